@@ -1,0 +1,315 @@
+// GEMM / MatMul entry points, the fp32 FFMA fallback GEMM, direct
+// convolution for small problems, and the GEMM dispatcher.
+//
+// Dispatch: a contraction with enough work and 16-byte aligned rows runs on
+// the tcgen05 3xTF32 kernel (gemm_tc.cu); everything else runs on an fp32
+// SIMT kernel whose per-output summation order (sequential over k, separate
+// multiply and add) is exactly the reference's mm_unsafe_vectorized order
+// (src/Lokad.Onnx.Tensors/MathOps.cs:380-410) -- bit-identical results on the
+// small shapes where launch latency, not the tensor pipe, is the bound.
+#include <vector>
+
+#include "lonnx_internal.cuh"
+
+namespace {
+
+constexpr int SB_M = 64, SB_N = 64, SB_K = 16;
+
+// C[b] = alpha * A[b] . op(B[b]) (+ beta*bias) (+ residual) -> epilogue
+template <bool TB>
+__global__ void __launch_bounds__(256)
+k_gemm_simt(const float *__restrict__ A, const float *__restrict__ B, const float *__restrict__ bias,
+            const float *__restrict__ res, float *__restrict__ C, int M, int N, int K, int64_t sA,
+            int64_t sB, int64_t sC, float alpha, float beta, int epi) {
+    __shared__ float As[SB_K][SB_M + 4];
+    __shared__ float Bs[SB_K][SB_N + 4];
+    const int b = blockIdx.z;
+    A += b * sA;
+    B += b * sB;
+    C += b * sC;
+    if (res) res += b * sC;
+    const int m0 = blockIdx.y * SB_M, n0 = blockIdx.x * SB_N;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < K; k0 += SB_K) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int e = threadIdx.x + 256 * t;  // 0..1023
+            {
+                const int kk = e & 15, mm = e >> 4;
+                const int gm = m0 + mm, gk = k0 + kk;
+                As[kk][mm] = (gm < M && gk < K) ? A[(int64_t)gm * K + gk] : 0.0f;
+            }
+            {
+                int kk, nn;
+                if (TB) { kk = e & 15; nn = e >> 4; } else { nn = e & 63; kk = e >> 6; }
+                const int gn = n0 + nn, gk = k0 + kk;
+                float v = 0.0f;
+                if (gn < N && gk < K) v = TB ? B[(int64_t)gn * K + gk] : B[(int64_t)gk * N + gn];
+                Bs[kk][nn] = v;
+            }
+        }
+        __syncthreads();
+        const int kmax = min(SB_K, K - k0);
+        for (int kk = 0; kk < kmax; ++kk) {
+            float a[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], bv[j]));
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int gm = m0 + ty + 16 * i;
+        if (gm >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int gn = n0 + tx + 16 * j;
+            if (gn >= N) continue;
+            float v = acc[i][j];
+            if (alpha != 1.0f) v = __fmul_rn(v, alpha);
+            if (bias) v = __fadd_rn(v, beta == 1.0f ? bias[gn] : __fmul_rn(beta, bias[gn]));
+            if (res) v = __fadd_rn(v, res[(int64_t)gm * N + gn]);
+            if (epi == LONNX_EPI_RELU) v = v > 0.0f ? v : 0.0f;
+            else if (epi == LONNX_EPI_GELU_ERF) v = lonnx_gelu_chain(v);
+            C[(int64_t)gm * N + gn] = v;
+        }
+    }
+}
+
+// Direct NCHW convolution, one thread per output element, summing over
+// (c, ky, kx) in the im2col row order of MathOps.Conv2D with a separate
+// multiply and add (MathOps.cs:821-846), then the bias pass (:862-872) and
+// an optional ReLU.  Padded taps are skipped (they add an exact zero).
+__global__ void k_conv2d_direct(const float *__restrict__ x, const float *__restrict__ w,
+                                const float *__restrict__ bias, float *__restrict__ y, int N, int C,
+                                int H, int W, int M, int kh, int kw, int sh, int sw, int pt, int pl,
+                                int dh, int dw, int group, int Ho, int Wo, int relu) {
+    const int64_t total = (int64_t)N * M * Ho * Wo;
+    const int cg = C / group, mg = M / group;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += stride) {
+        const int ox = (int)(t % Wo);
+        const int oy = (int)((t / Wo) % Ho);
+        const int m = (int)((t / ((int64_t)Wo * Ho)) % M);
+        const int n = (int)(t / ((int64_t)Wo * Ho * M));
+        const int g = m / mg;
+        const float *wp = w + (int64_t)m * cg * kh * kw;
+        float acc = 0.0f;
+        for (int c = 0; c < cg; ++c) {
+            const float *xp = x + ((int64_t)n * C + g * cg + c) * H * W;
+            for (int ky = 0; ky < kh; ++ky) {
+                const int iy = oy * sh - pt + ky * dh;
+                for (int kx = 0; kx < kw; ++kx) {
+                    const int ix = ox * sw - pl + kx * dw;
+                    if (iy < 0 || iy >= H || ix < 0 || ix >= W) continue;
+                    acc = __fadd_rn(acc, __fmul_rn(wp[(c * kh + ky) * kw + kx], xp[(int64_t)iy * W + ix]));
+                }
+            }
+        }
+        if (bias) acc = __fadd_rn(acc, bias[m]);
+        if (relu) acc = acc > 0.0f ? acc : 0.0f;
+        y[t] = acc;
+    }
+}
+
+inline int grid_for(lonnx_ctx *ctx, int64_t work, int threads = 256) {
+    int64_t blocks = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)ctx->num_sms * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (int)blocks;
+}
+
+inline bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+}  // namespace
+
+namespace lonnx {
+
+int transpose_launch(lonnx_ctx *ctx, const void *x, int elem_bytes, const int64_t *shape, int rank,
+                     const int64_t *perm, void *y);
+
+int gemm_simt(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
+              int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
+              float alpha, float beta, int epi, const float *residual) {
+    dim3 grid((N + SB_N - 1) / SB_N, (M + SB_M - 1) / SB_M, batch);
+    if (grid.z > 65535) return set_error(LONNX_E_UNSUPPORTED, "gemm: batch %d too large", batch);
+    if (transB)
+        k_gemm_simt<true><<<grid, 256, 0, ctx->stream>>>(A, B, bias, residual, C, M, N, K, sA, sB, sC, alpha, beta, epi);
+    else
+        k_gemm_simt<false><<<grid, 256, 0, ctx->stream>>>(A, B, bias, residual, C, M, N, K, sA, sB, sC, alpha, beta, epi);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+// Minimum work (multiply-adds) before the tensor-core path pays off.
+static int64_t tc_min_work() {
+    static int64_t v = [] {
+        const char *e = getenv("LONNX_TC_MIN_WORK");
+        return e ? atoll(e) : (int64_t)1 << 21;
+    }();
+    return v;
+}
+
+int gemm_dispatch(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
+                  int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
+                  float alpha, float beta, int epi, const float *residual) {
+    if (M == 0 || N == 0 || batch == 0) return LONNX_OK;
+    if (K == 0) {
+        // empty contraction: C = beta*bias (+ epilogue); the SIMT kernel handles it
+        return gemm_simt(ctx, A, B, bias, C, batch, M, N, K, sA, sB, sC, transB, alpha, beta, epi, residual);
+    }
+    // a shared weight with a dense batch of A folds into one tall GEMM
+    if (batch > 1 && sB == 0 && sA == (int64_t)M * K && sC == (int64_t)M * N && (int64_t)batch * M < (1ll << 31)) {
+        M *= batch;
+        batch = 1;
+    }
+    const bool big = (int64_t)M * N * K >= tc_min_work();
+    const bool aligned = (K % 4 == 0) && al16(A) && al16(B) && (sA % 4 == 0) && (sB % 4 == 0) &&
+                         (transB || N % 4 == 0);
+    static const bool tc_off = getenv("LONNX_DISABLE_TC") != nullptr;
+    if (big && aligned && !residual && !tc_off) {
+        const float *W = B;
+        int64_t sW = sB;
+        if (!transB) {
+            // tensor-core operands are K-major: transpose B[b] (K x N) -> (N x K)
+            void *tmp = nullptr;
+            const int nb = sB == 0 ? 1 : batch;
+            int rc = ctx_scratch(ctx, (size_t)nb * K * N * sizeof(float), &tmp);
+            if (rc) return rc;
+            for (int b = 0; b < nb; ++b) {
+                const int64_t shp[2] = {K, N}, perm[2] = {1, 0};
+                rc = transpose_launch(ctx, B + b * sB, 4, shp, 2, perm, (float *)tmp + (int64_t)b * K * N);
+                if (rc) return rc;
+            }
+            W = (const float *)tmp;
+            sW = sB == 0 ? 0 : (int64_t)K * N;
+        }
+        for (int b = 0; b < batch; ++b) {
+            int rc = gemm_tc(ctx, A + b * sA, W + b * sW, bias, nullptr, C + b * sC, M, N, K, K, K, N,
+                             alpha, beta, epi);
+            if (rc == LONNX_E_UNSUPPORTED) break;  // fall through to SIMT for all
+            if (rc) return rc;
+            if (b == batch - 1) return LONNX_OK;
+        }
+    }
+    return gemm_simt(ctx, A, B, bias, C, batch, M, N, K, sA, sB, sC, transB, alpha, beta, epi, residual);
+}
+
+}  // namespace lonnx
+
+using namespace lonnx;
+
+extern "C" {
+
+LONNX_API int lonnx_gemm_f32(lonnx_ctx *ctx, const float *A, const float *B, const float *bias,
+                             float *C, int batch, int M, int N, int K, int64_t strideA,
+                             int64_t strideB, int64_t strideC, int transB, float alpha, float beta,
+                             int epilogue) {
+    int rc = device_guard(ctx);
+    if (rc) return rc;
+    if (!A || !B || !C || batch < 0 || M < 0 || N < 0 || K < 0 || epilogue < 0 || epilogue > 2)
+        return set_error(LONNX_E_BADARG, "gemm: bad arguments");
+    return gemm_dispatch(ctx, A, B, bias, C, batch, M, N, K, strideA, strideB, strideC, transB, alpha,
+                         beta, epilogue, nullptr);
+}
+
+LONNX_API int lonnx_matmul_f32(lonnx_ctx *ctx, const float *a, const int64_t *as, int ar,
+                               const float *b, const int64_t *bs, int br, float *y) {
+    int rc = device_guard(ctx);
+    if (rc) return rc;
+    if (!a || !b || !y || ar < 1 || br < 1 || ar > 8 || br > 8)
+        return set_error(LONNX_E_BADARG, "The rank of each tensor in matrix multiplication must be greater than 1.");
+    if (ar == 1 && br == 1) {
+        if (as[0] != bs[0]) return set_error(LONNX_E_SHAPE, "MatMul: inner dimensions differ");
+        return gemm_dispatch(ctx, a, b, nullptr, y, 1, 1, 1, (int)as[0], 0, 0, 0, 0, 1.0f, 0.0f, 0, nullptr);
+    }
+    if (ar < 2 || br < 2)
+        return set_error(LONNX_E_UNSUPPORTED, "MatMul of a rank-1 and a rank>=2 tensor");
+    const int64_t m = as[ar - 2], k = as[ar - 1], k2 = bs[br - 2], n = bs[br - 1];
+    if (k != k2)
+        return set_error(LONNX_E_SHAPE, "The number of columns in the first matrix (%lld) is not equal to the number of rows in the second matrix (%lld).",
+                         (long long)k, (long long)k2);
+    int64_t lead[8];
+    int lr = 0;
+    rc = lonnx_broadcast_shape(as, ar - 2, bs, br - 2, lead, &lr);
+    if (rc) return set_error(LONNX_E_SHAPE, "The tensor shapes are not compatible for broadcasting.");
+    int64_t nb = 1;
+    for (int i = 0; i < lr; ++i) nb *= lead[i];
+    if (nb == 0 || m == 0 || n == 0) return LONNX_OK;
+    // per-dimension batch strides (0 where broadcast)
+    int64_t sa[8], sb[8];
+    {
+        int64_t s1 = m * k, s2 = k * n;
+        for (int d = lr - 1; d >= 0; --d) {
+            const int ia = d - (lr - (ar - 2)), ib = d - (lr - (br - 2));
+            const int64_t da = ia >= 0 ? as[ia] : 1, db = ib >= 0 ? bs[ib] : 1;
+            sa[d] = (da == 1) ? 0 : s1;
+            sb[d] = (db == 1) ? 0 : s2;
+            s1 *= da;
+            s2 *= db;
+        }
+    }
+    // uniform strides over the flattened batch? (dense or fully broadcast operand)
+    auto uniform = [&](const int64_t *s, int64_t unit) {
+        bool all0 = true, dense = true;
+        int64_t expect = unit;
+        for (int d = lr - 1; d >= 0; --d) {
+            all0 &= s[d] == 0;
+            dense &= (s[d] == expect) || lead[d] == 1;
+            expect *= lead[d];
+        }
+        return all0 ? 0 : (dense ? 1 : -1);
+    };
+    const int ua = uniform(sa, m * k), ub = uniform(sb, k * n);
+    if (ua >= 0 && ub >= 0)
+        return gemm_dispatch(ctx, a, b, nullptr, y, (int)nb, (int)m, (int)n, (int)k, ua ? m * k : 0,
+                             ub ? k * n : 0, m * n, 0, 1.0f, 0.0f, 0, nullptr);
+    // mixed broadcasting: one launch per batch index
+    for (int64_t i = 0; i < nb; ++i) {
+        int64_t rem = i, oa = 0, ob = 0;
+        for (int d = lr - 1; d >= 0; --d) {
+            const int64_t c = rem % lead[d];
+            rem /= lead[d];
+            oa += c * sa[d];
+            ob += c * sb[d];
+        }
+        rc = gemm_dispatch(ctx, a + oa, b + ob, nullptr, y + i * m * n, 1, (int)m, (int)n, (int)k, 0, 0, 0, 0,
+                           1.0f, 0.0f, 0, nullptr);
+        if (rc) return rc;
+    }
+    return LONNX_OK;
+}
+
+LONNX_API int lonnx_conv2d_f32(lonnx_ctx *ctx, const float *x, const float *w, const float *bias,
+                               float *y, int N, int C, int H, int W, int M, int kh, int kw, int sh,
+                               int sw, int pt, int pl, int pb, int pr, int dh, int dw, int group,
+                               int relu) {
+    int rc = device_guard(ctx);
+    if (rc) return rc;
+    if (!x || !w || !y || N < 0 || C <= 0 || M <= 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 ||
+        dh <= 0 || dw <= 0 || group <= 0 || C % group || M % group)
+        return set_error(LONNX_E_BADARG, "conv2d: bad arguments");
+    const int Ho = (H + pt + pb - (dh * (kh - 1) + 1)) / sh + 1;
+    const int Wo = (W + pl + pr - (dw * (kw - 1) + 1)) / sw + 1;
+    if (Ho <= 0 || Wo <= 0) return set_error(LONNX_E_SHAPE, "conv2d: empty output");
+    const int64_t total = (int64_t)N * M * Ho * Wo;
+    if (total == 0) return LONNX_OK;
+    k_conv2d_direct<<<grid_for(ctx, total), 256, 0, ctx->stream>>>(x, w, bias, y, N, C, H, W, M, kh, kw, sh, sw, pt,
+                                                                     pl, dh, dw, group, Ho, Wo, relu);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+}  // extern "C"

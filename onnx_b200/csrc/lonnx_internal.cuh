@@ -1,0 +1,106 @@
+// Internal declarations shared by the liblonnx_cuda translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "../../include/lonnx.h"
+
+namespace lonnx {
+
+// Device-side error flags, one int each, read and cleared by lonnx_sync().
+enum DevFlag { FLAG_OOB = 0, FLAG_TIMEOUT = 1, FLAG_COUNT = 4 };
+
+struct Allocator {
+    // Caching allocator: freed blocks are kept per exact rounded size and
+    // reused, so a graph that runs repeatedly reaches a steady state with no
+    // cudaMalloc/cudaFree on the execute path.
+    std::multimap<size_t, void *> free_blocks;
+    std::unordered_map<void *, size_t> live;
+    size_t bytes_reserved = 0;
+    size_t limit = 0;  // 0 = none; LONNX_MEM_LIMIT (bytes) caps reservations
+};
+
+}  // namespace lonnx
+
+struct lonnx_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int *dev_flags = nullptr;  // FLAG_COUNT ints
+    int num_sms = 148;
+    lonnx::Allocator alloc;
+    int64_t launches = 0;
+    // scratch used by ops that need a temporary (e.g. the split/transposed B
+    // operand of a tensor-core GEMM); grown on demand, owned by the context
+    void *scratch = nullptr;
+    size_t scratch_bytes = 0;
+};
+
+namespace lonnx {
+
+int set_error(int code, const char *fmt, ...);
+int cuda_error(cudaError_t e, const char *what);
+#define LONNX_CUDA(call)                                              \
+    do {                                                              \
+        cudaError_t e_ = (call);                                      \
+        if (e_ != cudaSuccess) return ::lonnx::cuda_error(e_, #call); \
+    } while (0)
+#define LONNX_CHECK_LAUNCH(ctx)                                              \
+    do {                                                                     \
+        (ctx)->launches++;                                                   \
+        cudaError_t e_ = cudaGetLastError();                                 \
+        if (e_ != cudaSuccess) return ::lonnx::cuda_error(e_, "kernel launch"); \
+    } while (0)
+
+int ctx_alloc(lonnx_ctx *ctx, size_t bytes, void **out);
+int ctx_free(lonnx_ctx *ctx, void *p);
+int ctx_scratch(lonnx_ctx *ctx, size_t bytes, void **out);
+int device_guard(lonnx_ctx *ctx);
+
+// kernels implemented in other translation units (device pointers, ctx stream)
+int gemm_dispatch(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
+                  int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
+                  float alpha, float beta, int epi, const float *residual);
+// Tensor-core GEMM: C = A . W^T with W given K-major ([N, K] row-major);
+// returns LONNX_E_UNSUPPORTED when the shape does not fit its constraints.
+int gemm_tc(lonnx_ctx *ctx, const float *A, const float *W, const float *bias,
+            const float *residual, float *C, int M, int N, int K, int lda, int ldw, int ldc,
+            float alpha, float beta, int epi);
+int gemm_simt(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
+              int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
+              float alpha, float beta, int epi, const float *residual);
+
+}  // namespace lonnx
+
+// Numerics shared by kernels -------------------------------------------------
+
+// Abramowitz & Stegun 7.1.26 (the reference's MathOps.Erf,
+// src/Lokad.Onnx.Tensors/MathOps.cs:989-1010), evaluated in float with expf.
+__device__ __forceinline__ float lonnx_erf_as(float x) {
+    const float a1 = 0.254829592f, a2 = -0.284496736f, a3 = 1.421413741f;
+    const float a4 = -1.453152027f, a5 = 1.061405429f, p = 0.3275911f;
+    const float s = x < 0.0f ? -1.0f : 1.0f;
+    x = fabsf(x);
+    const float t = __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(p, x)));
+    float poly = __fadd_rn(__fmul_rn(a5, t), a4);
+    poly = __fadd_rn(__fmul_rn(poly, t), a3);
+    poly = __fadd_rn(__fmul_rn(poly, t), a2);
+    poly = __fadd_rn(__fmul_rn(poly, t), a1);
+    const float e = expf(__fmul_rn(-x, x));
+    const float y = __fsub_rn(1.0f, __fmul_rn(__fmul_rn(poly, t), e));
+    return s * y;
+}
+
+// GELU as the exported node chain computes it: Div(x, sqrt 2) -> Erf ->
+// Add(1) -> Mul(x) -> Mul(0.5), each step rounded to float.
+__device__ __forceinline__ float lonnx_gelu_chain(float x) {
+    const float a = __fdiv_rn(x, 1.41421353816986083984375f);
+    const float e = lonnx_erf_as(a);
+    const float c = __fadd_rn(e, 1.0f);
+    return __fmul_rn(__fmul_rn(x, c), 0.5f);
+}

@@ -1,0 +1,368 @@
+// Row kernels: softmax, LayerNorm, reductions, MaxPool.
+//
+// All HBM-bound.  A row of the innermost axis is owned by one warp and kept in
+// registers between passes, so each element is read from HBM once and written
+// once (the reference makes 6 full passes for Softmax, TensorOps.cs:1312-1330,
+// and 9 node passes for a LayerNorm).  Reductions over a middle axis use one
+// thread per output column so that the loads stay coalesced.
+#include <float.h>
+
+#include "lonnx_internal.cuh"
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+inline int grid_for(lonnx_ctx *ctx, int64_t work, int threads = 256) {
+    int64_t blocks = (work + threads - 1) / threads;
+    const int64_t cap = (int64_t)ctx->num_sms * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (int)blocks;
+}
+
+// ---------------------------------------------------------------------------
+// Softmax along the innermost axis: one warp per row, row cached in registers
+// (VPT values per lane, len <= 32*VPT).  The running max starts at 0.0f like
+// the reference's ReduceMax (TensorOps.cs:1820); softmax is shift-invariant so
+// this only matters when every logit is very negative.
+template <int VPT>
+__global__ void k_softmax_lastdim(const float *__restrict__ x, float *__restrict__ y,
+                                  int64_t rows, int len) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const float *xr = x + r * len;
+        float v[VPT];
+        float m = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int c = lane + 32 * i;
+            v[i] = c < len ? xr[c] : -INFINITY;
+            m = fmaxf(m, v[i]);
+        }
+        m = warp_max(m);
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int c = lane + 32 * i;
+            v[i] = c < len ? expf(__fsub_rn(v[i], m)) : 0.0f;
+            s = __fadd_rn(s, v[i]);
+        }
+        s = warp_sum(s);
+        float *yr = y + r * len;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int c = lane + 32 * i;
+            if (c < len) yr[c] = __fdiv_rn(v[i], s);
+        }
+    }
+}
+
+// Softmax along a strided axis ([outer, len, inner], inner > 1) or a long
+// innermost axis: one thread per (outer, inner) column, three passes.
+__global__ void k_softmax_strided(const float *__restrict__ x, float *__restrict__ y,
+                                  int64_t outer, int64_t len, int64_t inner) {
+    const int64_t cols = outer * inner;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < cols; t += stride) {
+        const int64_t o = t / inner, in = t % inner;
+        const float *xp = x + o * len * inner + in;
+        float *yp = y + o * len * inner + in;
+        float m = 0.0f;
+        for (int64_t j = 0; j < len; ++j) m = fmaxf(m, xp[j * inner]);
+        float s = 0.0f;
+        for (int64_t j = 0; j < len; ++j) {
+            const float e = expf(__fsub_rn(xp[j * inner], m));
+            yp[j * inner] = e;
+            s = __fadd_rn(s, e);
+        }
+        for (int64_t j = 0; j < len; ++j) yp[j * inner] = __fdiv_rn(yp[j * inner], s);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm over the last axis, following the exported node chain step by
+// step in float: mean = sum(x)/n; d = x - mean; var = sum(d*d)/n;
+// y = d / sqrt(var + eps) * gamma + beta.  With `res`, x = a + res first (the
+// residual Add node that feeds the LayerNorm).
+template <int VPT>
+__global__ void k_layernorm(const float *__restrict__ x, const float *__restrict__ res,
+                            const float *__restrict__ gamma, const float *__restrict__ beta,
+                            float eps, float *__restrict__ y, int64_t rows, int cols) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const float fn = (float)cols;
+    for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+        const float *xr = x + r * cols;
+        const float *rr = res ? res + r * cols : nullptr;
+        float v[VPT];
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int c = lane + 32 * i;
+            float t = 0.0f;
+            if (c < cols) {
+                t = xr[c];
+                if (rr) t = __fadd_rn(t, rr[c]);
+            }
+            v[i] = t;
+            s = __fadd_rn(s, t);
+        }
+        const float mean = __fdiv_rn(warp_sum(s), fn);
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int c = lane + 32 * i;
+            v[i] = __fsub_rn(v[i], mean);
+            if (c < cols) q = __fadd_rn(q, __fmul_rn(v[i], v[i]));
+        }
+        const float var = __fdiv_rn(warp_sum(q), fn);
+        const float sd = __fsqrt_rn(__fadd_rn(var, eps));
+        float *yr = y + r * cols;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+            const int c = lane + 32 * i;
+            if (c < cols) yr[c] = __fadd_rn(__fmul_rn(__fdiv_rn(v[i], sd), gamma[c]), beta[c]);
+        }
+    }
+}
+
+// Generic LayerNorm for long rows: one block per row, values re-read from HBM.
+__global__ void k_layernorm_block(const float *__restrict__ x, const float *__restrict__ res,
+                                  const float *__restrict__ gamma, const float *__restrict__ beta,
+                                  float eps, float *__restrict__ y, int64_t rows, int cols) {
+    __shared__ float red[32];
+    const int64_t r = blockIdx.x;
+    if (r >= rows) return;
+    const float *xr = x + r * cols;
+    const float *rr = res ? res + r * cols : nullptr;
+    auto val = [&](int c) { return rr ? __fadd_rn(xr[c], rr[c]) : xr[c]; };
+    auto block_sum = [&](float v) {
+        v = warp_sum(v);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+        __syncthreads();
+        float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        if (threadIdx.x < 32) t = warp_sum(t);
+        if (threadIdx.x == 0) red[0] = t;
+        __syncthreads();
+        t = red[0];
+        __syncthreads();
+        return t;
+    };
+    float s = 0.0f;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) s = __fadd_rn(s, val(c));
+    const float mean = __fdiv_rn(block_sum(s), (float)cols);
+    float q = 0.0f;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        const float d = __fsub_rn(val(c), mean);
+        q = __fadd_rn(q, __fmul_rn(d, d));
+    }
+    const float sd = __fsqrt_rn(__fadd_rn(__fdiv_rn(block_sum(q), (float)cols), eps));
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        const float d = __fsub_rn(val(c), mean);
+        y[r * cols + c] = __fadd_rn(__fmul_rn(__fdiv_rn(d, sd), gamma[c]), beta[c]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Reductions.  op: 0 sum, 1 max (running max from 0.0f, as the reference's
+// ReduceMax, TensorOps.cs:1820), 2 mean (sum, then divide by the count).
+__device__ __forceinline__ float reduce_finish(int op, float acc, int64_t r) {
+    return op == LONNX_REDUCE_MEAN ? __fdiv_rn(acc, (float)r) : acc;
+}
+
+// [outer, r] -> [outer], one warp per row
+__global__ void k_reduce_rows(int op, const float *__restrict__ x, float *__restrict__ y,
+                              int64_t outer, int64_t r) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t o = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); o < outer; o += warps) {
+        const float *xr = x + o * r;
+        float acc = 0.0f;
+        if (op == LONNX_REDUCE_MAX) {
+            for (int64_t j = lane; j < r; j += 32) acc = fmaxf(acc, xr[j]);
+            acc = warp_max(acc);
+        } else {
+            for (int64_t j = lane; j < r; j += 32) acc = __fadd_rn(acc, xr[j]);
+            acc = warp_sum(acc);
+        }
+        if (lane == 0) y[o] = reduce_finish(op, acc, r);
+    }
+}
+
+// [outer, r, inner] -> [outer, inner], one thread per output, sequential in r
+__global__ void k_reduce_mid(int op, const float *__restrict__ x, float *__restrict__ y,
+                             int64_t outer, int64_t r, int64_t inner) {
+    const int64_t n = outer * inner;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += stride) {
+        const int64_t o = t / inner, in = t % inner;
+        const float *xp = x + o * r * inner + in;
+        float acc = 0.0f;
+        if (op == LONNX_REDUCE_MAX)
+            for (int64_t j = 0; j < r; ++j) acc = fmaxf(acc, xp[j * inner]);
+        else
+            for (int64_t j = 0; j < r; ++j) acc = __fadd_rn(acc, xp[j * inner]);
+        y[t] = reduce_finish(op, acc, r);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// MaxPool2D (TensorOps.cs:1025-1099): window clipped to the input, max from
+// -inf; the window ignores dilation as the reference's does.
+__global__ void k_maxpool2d(const float *__restrict__ x, float *__restrict__ y, int N, int C,
+                            int H, int W, int kh, int kw, int sh, int sw, int pt, int pl, int Ho,
+                            int Wo) {
+    const int64_t total = (int64_t)N * C * Ho * Wo;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += stride) {
+        const int ox = (int)(t % Wo);
+        const int oy = (int)((t / Wo) % Ho);
+        const int64_t nc = t / ((int64_t)Wo * Ho);
+        const float *xp = x + nc * H * W;
+        const int r0 = oy * sh - pt, c0 = ox * sw - pl;
+        const int rmin = max(r0, 0), rmax = min(r0 + kh, H);
+        const int cmin = max(c0, 0), cmax = min(c0 + kw, W);
+        float m = -INFINITY;
+        for (int r = rmin; r < rmax; ++r)
+            for (int c = cmin; c < cmax; ++c) m = fmaxf(m, xp[(int64_t)r * W + c]);
+        y[t] = m;
+    }
+}
+
+}  // namespace
+
+using namespace lonnx;
+
+namespace lonnx {
+// Reduction of a dense [outer, r, inner] view (no allocation).
+int reduce_view(lonnx_ctx *ctx, int op, const float *x, int64_t outer, int64_t r, int64_t inner,
+                float *y) {
+    if (inner == 1) {
+        k_reduce_rows<<<grid_for(ctx, outer * 32), 256, 0, ctx->stream>>>(op, x, y, outer, r);
+    } else {
+        k_reduce_mid<<<grid_for(ctx, outer * inner), 256, 0, ctx->stream>>>(op, x, y, outer, r, inner);
+    }
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+int transpose_launch(lonnx_ctx *ctx, const void *x, int elem_bytes, const int64_t *shape, int rank,
+                     const int64_t *perm, void *y);
+}  // namespace lonnx
+
+extern "C" {
+
+LONNX_API int lonnx_softmax_f32(lonnx_ctx *ctx, const float *x, float *y, int64_t outer,
+                                int64_t len, int64_t inner) {
+    int rc = device_guard(ctx);
+    if (rc) return rc;
+    if (!x || !y || outer < 0 || len < 0 || inner < 0) return set_error(LONNX_E_BADARG, "softmax: bad arguments");
+    if (outer * len * inner == 0) return LONNX_OK;
+    cudaStream_t st = ctx->stream;
+    if (inner == 1 && len <= 1024) {
+        const int64_t rows = outer;
+        const int g = grid_for(ctx, rows * 32);
+        if (len <= 128) k_softmax_lastdim<4><<<g, 256, 0, st>>>(x, y, rows, (int)len);
+        else if (len <= 512) k_softmax_lastdim<16><<<g, 256, 0, st>>>(x, y, rows, (int)len);
+        else k_softmax_lastdim<32><<<g, 256, 0, st>>>(x, y, rows, (int)len);
+    } else {
+        k_softmax_strided<<<grid_for(ctx, outer * inner), 256, 0, st>>>(x, y, outer, len, inner);
+    }
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+LONNX_API int lonnx_layernorm_f32(lonnx_ctx *ctx, const float *x, const float *res,
+                                  const float *gamma, const float *beta, float eps, float *y,
+                                  int64_t rows, int cols) {
+    int rc = device_guard(ctx);
+    if (rc) return rc;
+    if (!x || !gamma || !beta || !y || rows < 0 || cols <= 0) return set_error(LONNX_E_BADARG, "layernorm: bad arguments");
+    if (rows == 0) return LONNX_OK;
+    cudaStream_t st = ctx->stream;
+    const int g = grid_for(ctx, rows * 32);
+    if (cols <= 128) k_layernorm<4><<<g, 256, 0, st>>>(x, res, gamma, beta, eps, y, rows, cols);
+    else if (cols <= 384) k_layernorm<12><<<g, 256, 0, st>>>(x, res, gamma, beta, eps, y, rows, cols);
+    else if (cols <= 1024) k_layernorm<32><<<g, 256, 0, st>>>(x, res, gamma, beta, eps, y, rows, cols);
+    else k_layernorm_block<<<(unsigned)rows, 256, 0, st>>>(x, res, gamma, beta, eps, y, rows, cols);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+LONNX_API int lonnx_reduce_f32(lonnx_ctx *ctx, int op, const float *x, const int64_t *shape,
+                               int rank, const int64_t *axes, int naxes, float *y) {
+    int rc = device_guard(ctx);
+    if (rc) return rc;
+    if (!x || !y || rank < 0 || rank > 8 || naxes < 0 || naxes > rank || op < 0 || op > 2)
+        return set_error(LONNX_E_BADARG, "reduce: bad arguments");
+    bool red[8] = {false};
+    int ax[8];
+    int na = 0;
+    if (naxes == 0) {
+        for (int d = 0; d < rank; ++d) ax[na++] = d;
+    } else {
+        for (int i = 0; i < naxes; ++i) {
+            int a = (int)axes[i];
+            if (a < 0) a += rank;
+            if (a < 0 || a >= rank) return set_error(LONNX_E_BADARG, "reduce: axis %lld out of range", (long long)axes[i]);
+            if (red[a]) return set_error(LONNX_E_BADARG, "axes contains a repeated dimension.");
+            ax[na++] = a;
+        }
+    }
+    for (int i = 0; i < na; ++i) red[ax[i]] = true;
+    int64_t total = 1;
+    for (int d = 0; d < rank; ++d) total *= shape[d];
+    if (total == 0) return LONNX_OK;
+    // contiguous reduced block [lo, hi)?
+    int lo = rank, hi = -1;
+    for (int d = 0; d < rank; ++d)
+        if (red[d]) { lo = d < lo ? d : lo; hi = d > hi ? d : hi; }
+    bool contiguous = true;
+    for (int d = lo; d <= hi; ++d) contiguous &= red[d];
+    if (contiguous) {
+        int64_t outer = 1, r = 1, inner = 1;
+        for (int d = 0; d < lo; ++d) outer *= shape[d];
+        for (int d = lo; d <= hi; ++d) r *= shape[d];
+        for (int d = hi + 1; d < rank; ++d) inner *= shape[d];
+        return reduce_view(ctx, op, x, outer, r, inner, y);
+    }
+    // general: move the reduced axes innermost (in the given order, as
+    // ArrayUtilities.GetAxesPermutationForReduction does) into scratch
+    int64_t perm[8];
+    int np = 0;
+    int64_t outer = 1, r = 1;
+    for (int d = 0; d < rank; ++d)
+        if (!red[d]) { perm[np++] = d; outer *= shape[d]; }
+    for (int i = 0; i < na; ++i) { perm[np++] = ax[i]; r *= shape[ax[i]]; }
+    void *tmp = nullptr;
+    rc = ctx_scratch(ctx, (size_t)total * sizeof(float), &tmp);
+    if (rc) return rc;
+    rc = transpose_launch(ctx, x, 4, shape, rank, perm, tmp);
+    if (rc) return rc;
+    return reduce_view(ctx, op, (const float *)tmp, outer, r, 1, y);
+}
+
+LONNX_API int lonnx_maxpool2d_f32(lonnx_ctx *ctx, const float *x, float *y, int N, int C, int H,
+                                  int W, int kh, int kw, int sh, int sw, int pt, int pl, int Ho,
+                                  int Wo) {
+    int rc = device_guard(ctx);
+    if (rc) return rc;
+    if (!x || !y || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0) return set_error(LONNX_E_BADARG, "maxpool: bad arguments");
+    const int64_t total = (int64_t)N * C * Ho * Wo;
+    if (total <= 0) return LONNX_OK;
+    k_maxpool2d<<<grid_for(ctx, total), 256, 0, ctx->stream>>>(x, y, N, C, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,269 @@
+"""Per-op parity on the GPU: every op of the path, run through the provider
+(one-node graphs through liblonnx_cuda.so, the reference's run_node form,
+src/interop/backend.py:149-187) and through the direct C ABI, compared with
+the oracle on the same seeded inputs.  Data movement (Gather, Transpose,
+Reshape, Slice, Concat) must be bit-exact; float math within
+|gpu - ref| <= 1e-4 + 1e-4 |ref|."""
+import numpy as np
+import pytest
+
+from conftest import close
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def P():
+    from onnx_b200.provider import CUDAExecutionProvider
+    return CUDAExecutionProvider
+
+
+def ok(r):
+    assert r.Status == "Success", r.Message
+    return r.Outputs[0]
+
+
+@pytest.mark.parametrize("op", ["Add", "Sub", "Mul", "Div", "Pow"])
+@pytest.mark.parametrize("sa,sb", [((1, 8, 28, 28), (8, 1, 1)), ((64, 384), (384,)), ((384,), (64, 384)),
+                                   ((3, 4, 5), ()), ((), (3, 4, 5)), ((2, 12, 16, 16), (2, 1, 1, 16)),
+                                   ((5, 1, 7), (1, 6, 1)), ((37,), (37,))])
+def test_binary_broadcast(P, op, sa, sb):
+    rng = np.random.default_rng(hash((op, sa, sb)) % 2**32)
+    a = rng.uniform(0.5, 2.0, sa).astype(np.float32)
+    b = rng.uniform(0.5, 2.0, sb).astype(np.float32)
+    if op == "Pow":
+        b = np.full(sb, 2.0, np.float32)
+    got = ok(getattr(P, op)(a, b))
+    ref = O.binary(op, a, b)
+    assert got.shape == ref.shape
+    if op == "Pow":
+        assert np.array_equal(got, ref)
+    else:
+        assert np.array_equal(got, ref), "IEEE element-wise ops must match exactly"
+
+
+def test_binary_incompatible(P):
+    r = P.Add(np.zeros((3, 4), np.float32), np.zeros((5,), np.float32))
+    assert r.Status == "Failure" and "broadcast" in r.Message
+
+
+def test_binary_type_mismatch(P):
+    r = P.Add(np.zeros(3, np.float32), np.zeros(3, np.int64))
+    assert r.Status == "Failure"
+
+
+@pytest.mark.parametrize("op", ["Relu", "Sqrt", "Erf"])
+@pytest.mark.parametrize("n", [1, 5, 1000, 1 << 17])
+def test_unary(P, op, n):
+    rng = np.random.default_rng(n)
+    x = rng.uniform(-4, 4, n).astype(np.float32)
+    if op == "Sqrt":
+        x = np.abs(x)
+    got = ok(getattr(P, op)(x))
+    ref = O.unary(op, x)
+    if op == "Erf":
+        close(got, ref, atol=1e-6, rtol=1e-6)
+    else:
+        assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("shape,axis", [((3, 4, 5), 0), ((3, 4, 5), 1), ((3, 4, 5), 2), ((3, 4, 5), -1),
+                                        ((2, 12, 128, 128), -1), ((7, 1000), -1), ((4, 2000), 1), ((1, 3), -1)])
+def test_softmax(P, shape, axis):
+    rng = np.random.default_rng(len(shape) * 10 + axis)
+    x = (rng.standard_normal(shape) * 3).astype(np.float32)
+    close(ok(P.Softmax(x, axis)), O.softmax(x, axis), atol=1e-6, rtol=1e-5)
+
+
+def test_softmax_known_answers(P):
+    """tests/python/test_backend.py:815-827."""
+    y = ok(P.Softmax(np.array([[-1, 0, 1]], np.float32), None))
+    np.testing.assert_almost_equal(y, [[0.09003058, 0.24472848, 0.66524094]], decimal=7)
+    x = np.array([[0, 1, 2, 3], [10000, 10001, 10002, 10003]], np.float32)
+    e = [0.032058604, 0.08714432, 0.23688284, 0.6439143]
+    np.testing.assert_almost_equal(ok(P.Softmax(x, None)), [e, e], decimal=7)
+
+
+@pytest.mark.parametrize("op", ["ReduceSum", "ReduceMean", "ReduceMax"])
+@pytest.mark.parametrize("shape,axes,keep", [((4, 16, 384), [-1], 1), ((4, 16, 384), [1], 0), ((4, 16, 384), None, 1),
+                                             ((3, 4, 5, 6), [0, 2], 1), ((3, 4, 5, 6), [3, 1], 0),
+                                             ((2, 3), [0], 1)])
+def test_reduce(P, op, shape, axes, keep):
+    rng = np.random.default_rng(len(shape) + (len(axes) if axes else 0))
+    x = rng.standard_normal(shape).astype(np.float32)
+    got = ok(getattr(P, op)(x, axes, keep))
+    ref = {"ReduceSum": O.reduce_sum, "ReduceMean": O.reduce_mean, "ReduceMax": O.reduce_max}[op](x, axes, keep)
+    assert got.shape == ref.shape
+    close(got, ref, atol=1e-5, rtol=1e-5)
+
+
+def test_reducemax_starts_at_zero(P):
+    """Reference defect kept for parity: ReduceMax's running max starts at 0
+    (src/Lokad.Onnx.Tensors/TensorOps.cs:1820)."""
+    x = -np.ones((2, 3), np.float32)
+    assert np.array_equal(ok(P.ReduceMax(x, [1], 1)), np.zeros((2, 1), np.float32))
+
+
+def test_conv_known_answers(P):
+    """tests/Lokad.Onnx.Tensors.Tests/MathTests.cs:127-151 (ONNX Conv doc
+    values), via the conv kernel with explicit pads/strides."""
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import Context, DeviceTensor
+    ctx = Context.default(0)
+
+    def conv(x, w, pads, stride):
+        dx, dw = DeviceTensor.from_host(ctx, x), DeviceTensor.from_host(ctx, w)
+        H, W = x.shape[2:]
+        Ho = (H + 2 * pads - 3) // stride + 1
+        Wo = (W + 2 * pads - 3) // stride + 1
+        y = DeviceTensor(ctx, (1, 1, Ho, Wo), np.float32)
+        N.check(N.lib.lonnx_conv2d_f32(ctx.handle, dx.ptr, dw.ptr, None, y.ptr, 1, 1, H, W, 1, 3, 3, stride, stride,
+                                       pads, pads, pads, pads, 1, 1, 1, 0))
+        return y.to_host()
+
+    X = np.arange(25, dtype=np.float32).reshape(1, 1, 5, 5)
+    Wt = np.ones((1, 1, 3, 3), np.float32)
+    assert np.array_equal(conv(X, Wt, 1, 1)[0, 0], [[12, 21, 27, 33, 24], [33, 54, 63, 72, 51], [63, 99, 108, 117, 81],
+                                                    [93, 144, 153, 162, 111], [72, 111, 117, 123, 84]])
+    assert np.array_equal(conv(X, Wt, 0, 1)[0, 0], [[54, 63, 72], [99, 108, 117], [144, 153, 162]])
+    X7 = np.arange(35, dtype=np.float32).reshape(1, 1, 7, 5)
+    assert np.array_equal(conv(X7, Wt, 1, 2)[0, 0], [[12, 27, 24], [63, 108, 81], [123, 198, 141], [112, 177, 124]])
+
+
+@pytest.mark.parametrize("xs,ws,auto_pad", [((1, 1, 28, 28), (8, 1, 5, 5), "SAME_UPPER"),
+                                            ((1, 8, 14, 14), (16, 8, 5, 5), "SAME_UPPER"),
+                                            ((2, 3, 9, 11), (4, 3, 3, 3), "VALID"), ((2, 3, 9, 9), (4, 3, 3, 3), None)])
+def test_conv_provider_vs_oracle(P, xs, ws, auto_pad):
+    rng = np.random.default_rng(xs[1] * 10 + ws[0])
+    x = rng.uniform(0, 1, xs).astype(np.float32)
+    w = (rng.standard_normal(ws) * 0.1).astype(np.float32)
+    b = (rng.standard_normal(ws[0]) * 0.1).astype(np.float32)
+    got = ok(P.Conv(x, w, b, auto_pad=auto_pad))
+    ref = O.conv(x, w, b, auto_pad=auto_pad)
+    assert np.array_equal(got, ref), "direct conv follows the reference summation order exactly"
+
+
+def test_maxpool_known_answers(P):
+    """tests/Lokad.Onnx.Tensors.Tests/MathTests.cs:154-168."""
+    X = np.array([[[[12, 20, 30, 0], [8, 12, 2, 0], [34, 70, 37, 4], [112, 100, 25, 12]]]], np.float32)
+    y = ok(P.MaxPool(X, auto_pad="NOTSET", kernel_shape=[2, 2], pads=[0, 0, 0, 0], strides=[2, 2]))
+    assert np.array_equal(y[0, 0], [[20, 30], [112, 37]])
+    y = ok(P.MaxPool(X, auto_pad="NOTSET", kernel_shape=[2, 2], pads=[0, 0, 0, 0], strides=[1, 1]))
+    assert np.array_equal(y[0, 0], [[20, 30, 30], [70, 70, 37], [112, 100, 37]])
+
+
+@pytest.mark.parametrize("xs,k,s,ap,pads", [((1, 8, 28, 28), 2, 2, "NOTSET", [0, 0, 0, 0]),
+                                            ((1, 16, 14, 14), 3, 3, "NOTSET", [0, 0, 0, 0]),
+                                            ((2, 4, 11, 11), 3, 2, "NOTSET", [1, 1, 1, 1]),
+                                            ((2, 4, 10, 10), 3, 2, "SAME_UPPER", None)])
+def test_maxpool_vs_oracle(P, xs, k, s, ap, pads):
+    x = np.random.default_rng(k * s).standard_normal(xs).astype(np.float32)
+    got = ok(P.MaxPool(x, auto_pad=ap, kernel_shape=[k, k], pads=pads, strides=[s, s]))
+    ref = O.maxpool(x, auto_pad=ap, kernel_shape=[k, k], pads=pads, strides=[s, s])
+    assert np.array_equal(got, ref)
+
+
+def test_gather_reference_cases(P):
+    """tests/python/test_backend.py:379-442, including negative indices."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((10, 10)).astype(np.float32)
+    y = np.array([[0, 1], [1, 2]])
+    assert np.array_equal(ok(P.Gather(x, y)), np.take(x, y, axis=0))
+    assert np.array_equal(ok(P.Gather(x, np.array([[-10, -9], [1, -8]]))), np.take(x, y, axis=0))
+    data = rng.standard_normal((5, 4, 3, 2)).astype(np.float32)
+    for axis in (0, 1):
+        assert np.array_equal(ok(P.Gather(data, np.array([0, 1, 3]), axis)), np.take(data, [0, 1, 3], axis=axis))
+    d2 = rng.standard_normal((3, 3)).astype(np.float32)
+    assert np.array_equal(ok(P.Gather(d2, np.array([[0, 2]]), 1)), np.take(d2, [[0, 2]], axis=1))
+    d3 = np.arange(10, dtype=np.float32)
+    assert np.array_equal(ok(P.Gather(d3, np.array([0, -9, -10]), 0)), np.take(d3, [0, -9, -10]))
+
+
+def test_gather_embedding_rows_bit_exact(ctx):
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    rng = np.random.default_rng(2)
+    table = rng.standard_normal((50000, 384)).astype(np.float32)
+    idx = rng.integers(-50000, 50000, size=(32, 128)).astype(np.int64)
+    dt, di = DeviceTensor.from_host(ctx, table), DeviceTensor.from_host(ctx, idx)
+    y = DeviceTensor(ctx, (32, 128, 384), np.float32)
+    N.check(N.lib.lonnx_gather(ctx.handle, dt.ptr, 4, 1, 50000, 384, di.ptr, idx.size, y.ptr))
+    ctx.sync()
+    assert np.array_equal(y.to_host(), O.gather(table, idx, 0))
+
+
+def test_gather_out_of_range_reports_oob(ctx):
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    table = np.ones((10, 8), np.float32)
+    idx = np.array([1, 10], np.int64)
+    dt, di = DeviceTensor.from_host(ctx, table), DeviceTensor.from_host(ctx, idx)
+    y = DeviceTensor(ctx, (2, 8), np.float32)
+    N.check(N.lib.lonnx_gather(ctx.handle, dt.ptr, 4, 1, 10, 8, di.ptr, 2, y.ptr))
+    with pytest.raises(N.LonnxError) as e:
+        ctx.sync()
+    assert e.value.code == -6
+    ctx.sync()  # flag cleared; the context stays usable
+    out = y.to_host()
+    assert np.array_equal(out[0], np.ones(8)) and np.array_equal(out[1], np.zeros(8))
+
+
+@pytest.mark.parametrize("shape,perm", [((2, 128, 12, 32), [0, 2, 1, 3]), ((2, 128, 12, 32), [0, 2, 3, 1]),
+                                        ((3, 4), None), ((2, 3, 4, 5, 6), [4, 0, 3, 1, 2])])
+def test_transpose_bit_exact(P, shape, perm):
+    x = np.random.default_rng(1).standard_normal(shape).astype(np.float32)
+    assert np.array_equal(ok(P.Transpose(x, perm)), O.transpose(x, perm))
+
+
+def test_reshape_and_unsqueeze(P):
+    x = np.arange(24, dtype=np.float32).reshape(2, 3, 4)
+    assert ok(P.Reshape(x, np.array([0, -1], np.int64))).shape == (2, 12)
+    assert ok(P.Unsqueeze(x, [0, 3])).shape == (1, 2, 3, 1, 4)
+    r = P.Reshape(x, np.array([5, -1], np.int64))
+    assert r.Status == "Failure"
+
+
+def test_layernorm_direct(ctx):
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    rng = np.random.default_rng(4)
+    for rows, cols in [(1000, 384), (7, 100), (33, 1024), (5, 3000)]:
+        x = rng.standard_normal((rows, cols)).astype(np.float32)
+        r = rng.standard_normal((rows, cols)).astype(np.float32)
+        gm = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+        bt = (0.1 * rng.standard_normal(cols)).astype(np.float32)
+        eps = np.float32(1e-12)
+        s = O.binary("Add", x, r)
+        mean = O.reduce_mean(s, [-1], 1)
+        d = O.binary("Sub", s, mean)
+        var = O.reduce_mean(O.binary("Pow", d, np.float32(2)), [-1], 1)
+        ref = O.binary("Add", O.binary("Mul", O.binary("Div", d, O.unary("Sqrt", O.binary("Add", var, eps))), gm), bt)
+        dx, dr, dg, db = (DeviceTensor.from_host(ctx, a) for a in (x, r, gm, bt))
+        y = DeviceTensor(ctx, (rows, cols), np.float32)
+        N.check(N.lib.lonnx_layernorm_f32(ctx.handle, dx.ptr, dr.ptr, dg.ptr, db.ptr, eps, y.ptr, rows, cols))
+        ctx.sync()
+        close(y.to_host(), ref, atol=1e-5, rtol=1e-5)
+
+
+def test_attention_direct(ctx):
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    rng = np.random.default_rng(8)
+    B, S, h, dh = 3, 128, 12, 32
+    H = h * dh
+    qkv = rng.standard_normal((B, S, 3 * H)).astype(np.float32)
+    mask = np.zeros((B, 1, 1, S), np.float32)
+    mask[1, ..., 100:] = np.finfo(np.float32).min
+    q, k, v = qkv[..., :H], qkv[..., H:2 * H], qkv[..., 2 * H:]
+    split = lambda t, p: O.transpose(t.reshape(B, S, h, dh), p)
+    s = O.matmul(split(q, [0, 2, 1, 3]), split(k, [0, 2, 3, 1]))
+    p = O.softmax(O.binary("Add", O.binary("Div", s, np.float32(np.sqrt(dh))), mask), -1)
+    ref = O.transpose(O.matmul(p, split(v, [0, 2, 1, 3])), [0, 2, 1, 3]).reshape(B, S, H)
+    dq = DeviceTensor.from_host(ctx, qkv)
+    dm = DeviceTensor.from_host(ctx, mask)
+    out = DeviceTensor(ctx, (B, S, H), np.float32)
+    N.check(N.lib.lonnx_attention_f32(ctx.handle, dq.ptr, dq.ptr + 4 * H, dq.ptr + 8 * H, 3 * H, dm.ptr, out.ptr,
+                                      B, S, h, dh, np.float32(np.sqrt(dh))))
+    ctx.sync()
+    close(out.to_host(), ref, atol=1e-5, rtol=1e-5)
