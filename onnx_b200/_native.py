@@ -9,7 +9,7 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "liblonnx_cuda.so")
+LIB_PATH = os.environ.get("LONNX_LIBRARY") or os.path.join(_HERE, "liblonnx_cuda.so")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(f"{LIB_PATH} is missing: build it with `python -m onnx_b200.build` "
@@ -41,7 +41,7 @@ _SIGS = {
     "lonnx_gemm_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_i64,
                                c_i64, c_int, c_f32, c_f32, c_int]),
     "lonnx_matmul_f32": (c_int, [c_vp, c_vp, i64p, c_int, c_vp, i64p, c_int, c_vp]),
-    "lonnx_conv2d_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp] + [c_int] * 18),
+    "lonnx_conv2d_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp] + [c_int] * 17),
     "lonnx_softmax_f32": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64]),
     "lonnx_layernorm_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_f32, c_vp, c_i64, c_int]),
     "lonnx_reduce_f32": (c_int, [c_vp, c_int, c_vp, i64p, c_int, i64p, c_int, c_vp]),

@@ -154,7 +154,7 @@ int gemm_simt(lonnx_ctx *ctx, const float *A, const float *B, const float *bias,
 }
 
 // Minimum work (multiply-adds) before the tensor-core path pays off.
-static int64_t tc_min_work() {
+int64_t gemm_tc_min_work() {
     static int64_t v = [] {
         const char *e = getenv("LONNX_TC_MIN_WORK");
         return e ? atoll(e) : (int64_t)1 << 21;
@@ -175,31 +175,26 @@ int gemm_dispatch(lonnx_ctx *ctx, const float *A, const float *B, const float *b
         M *= batch;
         batch = 1;
     }
-    const bool big = (int64_t)M * N * K >= tc_min_work();
+    const bool big = (int64_t)M * N * K >= gemm_tc_min_work();
     const bool aligned = (K % 4 == 0) && al16(A) && al16(B) && (sA % 4 == 0) && (sB % 4 == 0) &&
                          (transB || N % 4 == 0);
     static const bool tc_off = getenv("LONNX_DISABLE_TC") != nullptr;
     if (big && aligned && !residual && !tc_off) {
-        const float *W = B;
-        int64_t sW = sB;
-        if (!transB) {
-            // tensor-core operands are K-major: transpose B[b] (K x N) -> (N x K)
-            void *tmp = nullptr;
-            const int nb = sB == 0 ? 1 : batch;
-            int rc = ctx_scratch(ctx, (size_t)nb * K * N * sizeof(float), &tmp);
+        // tensor-core operands: B[b] split into K-major tf32 high/low parts in scratch
+        const int nb = sB == 0 ? 1 : batch;
+        void *tmp = nullptr;
+        int rc = ctx_scratch(ctx, (size_t)nb * 2 * K * N * sizeof(float), &tmp);
+        if (rc) return rc;
+        float *hi = (float *)tmp, *lo = hi + (size_t)nb * K * N;
+        for (int b = 0; b < nb; ++b) {
+            rc = split_tf32_nk(ctx, B + b * sB, hi + (int64_t)b * K * N, lo + (int64_t)b * K * N, K, N, transB);
             if (rc) return rc;
-            for (int b = 0; b < nb; ++b) {
-                const int64_t shp[2] = {K, N}, perm[2] = {1, 0};
-                rc = transpose_launch(ctx, B + b * sB, 4, shp, 2, perm, (float *)tmp + (int64_t)b * K * N);
-                if (rc) return rc;
-            }
-            W = (const float *)tmp;
-            sW = sB == 0 ? 0 : (int64_t)K * N;
         }
+        const int64_t sW = sB == 0 ? 0 : (int64_t)K * N;
         for (int b = 0; b < batch; ++b) {
-            int rc = gemm_tc(ctx, A + b * sA, W + b * sW, bias, nullptr, C + b * sC, M, N, K, K, K, N,
-                             alpha, beta, epi);
-            if (rc == LONNX_E_UNSUPPORTED) break;  // fall through to SIMT for all
+            rc = gemm_tc(ctx, A + b * sA, hi + b * sW, lo + b * sW, bias, C + b * sC, M, N, K, K, K, N, alpha, beta,
+                         epi);
+            if (rc == LONNX_E_UNSUPPORTED && b == 0) break;  // fall through to SIMT
             if (rc) return rc;
             if (b == batch - 1) return LONNX_OK;
         }

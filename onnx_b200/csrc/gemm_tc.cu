@@ -5,23 +5,24 @@
 //
 // Both operands are K-major (row-major A; the weight stored as [N, K]).  Each
 // operand element x is split into hi = x with the low 13 mantissa bits
-// cleared (exactly representable in tf32) and lo = x - hi (exact in fp32),
-// and the tile product accumulates hi.hi + hi.lo + lo.hi in fp32 TMEM -- the
-// published 3xTF32 scheme, which keeps fp32-level accuracy (the dropped
-// lo.lo term is ~2^-22 relative).  The split is done in shared memory right
-// after the TMA load, so HBM traffic is that of a plain fp32 GEMM.
+// cleared (exactly representable in tf32) and lo = x - hi (exact in fp32);
+// the tile product accumulates hi.hi + hi.lo + lo.hi -- the published 3xTF32
+// scheme, which keeps fp32-level accuracy (the dropped lo.lo term is ~2^-22
+// relative).  The weight is split once, ahead of time (split_tf32_nk); the
+// activation tile is split in shared memory right after its TMA load, so HBM
+// traffic for A is that of a plain fp32 GEMM.
 //
-// CTA = 8 warps, one 128 x BN output tile:
-//   warp 0      TMA producer (one lane): A and W tiles of 32 K-columns
-//               (128 bytes = one 128B-swizzle row) per stage
-//   warp 1      TMEM allocator + MMA issuer (one lane): 4 K-steps of 8 x
-//               3 products per stage, tcgen05.commit frees the stage
-//   warps 4..7  split the stage into hi/lo (128 threads), then run the
-//               epilogue: tcgen05.ld of their 32 TMEM lanes, bias and
-//               activation, fp32 stores
+// CTA = 12 warps, one 128 x BN output tile (BN = 128 or 192):
+//   warp 0      TMA producer (one lane): A, W_hi, W_lo tiles of 32 K-columns
+//               (128 bytes = one 128B-swizzle row) per stage, 3-4 stages
+//   warp 1      TMEM allocator + MMA issuer (one lane): 4 K-steps x 3
+//               products per stage into one of two TMEM chunk accumulators
+//   warps 2-3   write A_lo of each stage into a 2-buffer ring
+//   warps 4-11  drain each chunk accumulator into fp32 registers (round to
+//               nearest), then run the epilogue: bias, activation, stores
 // Every mbarrier wait is bounded (~2 s); on expiry the CTA raises an abort
-// flag, records LONNX_E_TIMEOUT in the context's device flags, drains and
-// frees its TMEM, and returns.
+// flag, records LONNX_E_TIMEOUT in the context's device flags, drains its
+// in-flight copies and MMAs, frees its TMEM, and returns.
 //
 // Replaces MathOps.mm_unsafe_vectorized (src/Lokad.Onnx.Tensors/MathOps.cs:380-410).
 #include <cuda.h>
@@ -39,46 +40,64 @@ using namespace lonnx::tc;
 constexpr int BM = 128;
 constexpr int BK = 32;                  // fp32 elements per 128-byte row
 constexpr int A_TILE = BM * BK * 4;     // 16 KB
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;           // 12 warps
+// warp roles: 0 TMA, 1 MMA + TMEM owner, 2-3 split A, 4-11 accumulate/epilogue
+constexpr int W_TMA = 0, W_MMA = 1, W_SPLIT0 = 2, N_SPLIT = 2, W_ACC0 = 4, N_ACC = 8;
 
 template <int BN>
 struct Cfg {
     static constexpr int W_TILE = BN * BK * 4;
-    static constexpr int STAGE = 2 * A_TILE + 2 * W_TILE;  // A, A_lo, W, W_lo
-    static constexpr int STAGES = (BN == 256) ? 2 : 3;
-    static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
-    static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+    static constexpr int STAGE = A_TILE + 2 * W_TILE;  // TMA ring: A, W_hi, W_lo
+    static constexpr int LO = 2 * A_TILE;              // A_lo ring: 2 buffers
+    static constexpr int STAGES = (4 * STAGE + LO + 1280 <= 227 * 1024) ? 4
+                                  : (3 * STAGE + LO + 1280 <= 227 * 1024) ? 3 : 2;
+    static constexpr int SMEM = STAGES * STAGE + LO + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;  // two chunk accumulators
+    static constexpr int COLS_PER_ACC = BN / 2;                  // per accumulator thread
 };
 
-__device__ __forceinline__ void split_tf32(float4 v, float4 &hi, float4 &lo) {
-    auto h = [](float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); };
-    hi = make_float4(h(v.x), h(v.y), h(v.z), h(v.w));
-    lo = make_float4(__fsub_rn(v.x, hi.x), __fsub_rn(v.y, hi.y), __fsub_rn(v.z, hi.z), __fsub_rn(v.w, hi.w));
-}
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
-// in place: buf <- hi(buf), lo_buf <- lo(buf); `bytes` multiple of 16*128
-__device__ __forceinline__ void split_tile(uint8_t *buf, uint8_t *lo_buf, int bytes, int tid) {
-    for (int off = tid * 16; off < bytes; off += 128 * 16) {
-        float4 v = *reinterpret_cast<float4 *>(buf + off);
-        float4 h, l;
-        split_tf32(v, h, l);
-        *reinterpret_cast<float4 *>(buf + off) = h;
+// lo_buf <- x - tf32(x).  The tensor core reads an fp32 operand as its tf32
+// truncation (tests/test_gemm_gpu.py::test_tf32_operand_truncation), so the
+// raw tile already serves as the high part.
+__device__ __forceinline__ void split_lo(const uint8_t *buf, uint8_t *lo_buf, int bytes, int tid, int nthreads) {
+#pragma unroll 4
+    for (int off = tid * 16; off < bytes; off += nthreads * 16) {
+        const float4 v = *reinterpret_cast<const float4 *>(buf + off);
+        float4 l;
+        l.x = __fsub_rn(v.x, tf32_hi(v.x));
+        l.y = __fsub_rn(v.y, tf32_hi(v.y));
+        l.z = __fsub_rn(v.z, tf32_hi(v.z));
+        l.w = __fsub_rn(v.w, tf32_hi(v.w));
         *reinterpret_cast<float4 *>(lo_buf + off) = l;
     }
 }
 
+// Accumulation: each K stage is accumulated by the tensor core into a fresh
+// TMEM buffer (two buffers, ping-pong) and the stage sums are added into fp32
+// registers with round-to-nearest by the accumulator warps.  The tensor
+// core's accumulator rounds toward zero, so one TMEM accumulator over all of
+// K builds an error that grows linearly with K (measured ~10x the
+// sequential fp32 sum at K = 1536); 32-wide chunks keep it at fp32 level.
+//
+// Shared-memory bandwidth is the binding resource of a 3xTF32 tile (operand
+// reads of three MMAs + TMA writes + the split), which is why the weight is
+// split once ahead of time and A_lo has its own 2-buffer ring (so the TMA
+// ring can be 3-4 stages deep).
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-              const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, int ldc,
-              float alpha, float beta, int epi, int *dev_flags) {
+              const __grid_constant__ CUtensorMap tmWlo, const float *__restrict__ bias, float *__restrict__ C,
+              int M, int N, int K, int ldc, float alpha, float beta, int epi, int *dev_flags) {
     using G = Cfg<BN>;
+    constexpr int S = G::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + G::STAGES * G::STAGE);
-    // bars[0..S): full (TMA landed), [S..2S): split done, [2S..3S): empty (MMA done),
-    // [3S]: accumulator ready, [3S+1]: drain on abort
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * G::STAGES + 2);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * G::STAGE + G::LO);
+    // [0,S) full  [S,2S) split done  [2S,3S) stage free  [3S,3S+2) chunk ready
+    // [3S+2,3S+4) chunk drained  [3S+4] abort drain  [3S+5,3S+7) A_lo buffer free
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 7);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -86,30 +105,37 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     const int nk = (K + BK - 1) / BK;
 
     auto full = [&](int s) { return smem_u32(bars + s); };
-    auto conv = [&](int s) { return smem_u32(bars + G::STAGES + s); };
-    auto empty = [&](int s) { return smem_u32(bars + 2 * G::STAGES + s); };
-    const uint32_t accbar = smem_u32(bars + 3 * G::STAGES);
-    const uint32_t drainbar = smem_u32(bars + 3 * G::STAGES + 1);
-    int issued = 0;  // TMA stage loads issued (producer lane)
+    auto conv = [&](int s) { return smem_u32(bars + S + s); };
+    auto empty = [&](int s) { return smem_u32(bars + 2 * S + s); };
+    auto tfull = [&](int b) { return smem_u32(bars + 3 * S + b); };
+    auto tdrain = [&](int b) { return smem_u32(bars + 3 * S + 2 + b); };
+    const uint32_t drainbar = smem_u32(bars + 3 * S + 4);
+    auto lofree = [&](int b) { return smem_u32(bars + 3 * S + 5 + b); };
     auto stageA = [&](int s) { return smem + s * G::STAGE; };
-    auto stageAlo = [&](int s) { return smem + s * G::STAGE + A_TILE; };
-    auto stageW = [&](int s) { return smem + s * G::STAGE + 2 * A_TILE; };
-    auto stageWlo = [&](int s) { return smem + s * G::STAGE + 2 * A_TILE + G::W_TILE; };
+    auto stageW = [&](int s) { return smem + s * G::STAGE + A_TILE; };
+    auto stageWlo = [&](int s) { return smem + s * G::STAGE + A_TILE + G::W_TILE; };
+    auto bufAlo = [&](int b) { return smem + S * G::STAGE + b * A_TILE; };
+    int issued = 0;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < G::STAGES; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(full(s), 1);
-            mbar_init(conv(s), 4);  // one arrive per splitting warp
+            mbar_init(conv(s), N_SPLIT);
             mbar_init(empty(s), 1);
         }
-        mbar_init(accbar, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull(b), 1);
+            mbar_init(tdrain(b), N_ACC);
+            mbar_init(lofree(b), 1);
+        }
         mbar_init(drainbar, 1);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmW);
+        prefetch_tmap(&tmWlo);
     }
-    if (warp == 1) {
+    if (warp == W_MMA) {
         tmem_alloc(smem_u32(tmem_slot), G::TMEM_COLS);
         tmem_relinquish();
     }
@@ -119,89 +145,107 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
 
-    if (warp == 0) {
+    if (warp == W_TMA) {
         if (lane == 0) {
+            constexpr uint32_t bytes = A_TILE + 2 * G::W_TILE;
             for (int i = 0; i < nk && ok; ++i) {
-                const int s = i % G::STAGES;
-                const uint32_t ph = (i / G::STAGES) & 1;
-                if (!mbar_wait(empty(s), ph ^ 1, abort_flag)) { ok = false; break; }
-                mbar_arrive_expect_tx(full(s), A_TILE + G::W_TILE);
+                const int s = i % S;
+                if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                mbar_arrive_expect_tx(full(s), bytes);
                 tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), i * BK, m0);
                 tma_load_2d(smem_u32(stageW(s)), &tmW, full(s), i * BK, n0);
+                tma_load_2d(smem_u32(stageWlo(s)), &tmWlo, full(s), i * BK, n0);
                 issued = i + 1;
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == W_MMA) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(BM, BN);
             for (int i = 0; i < nk && ok; ++i) {
-                const int s = i % G::STAGES;
-                const uint32_t ph = (i / G::STAGES) & 1;
-                if (!mbar_wait(conv(s), ph, abort_flag)) { ok = false; break; }
+                const int s = i % S, b = i & 1;
+                if (!mbar_wait(conv(s), (i / S) & 1, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(tdrain(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t a = smem_u32(stageA(s)), alo = smem_u32(stageAlo(s));
+                const uint32_t acc = tmem + b * BN;
+                const uint32_t a = smem_u32(stageA(s)), alo = smem_u32(bufAlo(b));
                 const uint32_t w = smem_u32(stageW(s)), wlo = smem_u32(stageWlo(s));
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
                     const uint32_t ko = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
                     const uint64_t da = smem_desc_sw128(a + ko), dal = smem_desc_sw128(alo + ko);
                     const uint64_t dw = smem_desc_sw128(w + ko), dwl = smem_desc_sw128(wlo + ko);
-                    mma_tf32(tmem, dal, dw, idesc, (i | kk) != 0);
-                    mma_tf32(tmem, da, dwl, idesc, 1);
-                    mma_tf32(tmem, da, dw, idesc, 1);
+                    mma_tf32(acc, dal, dw, idesc, kk != 0);
+                    mma_tf32(acc, da, dwl, idesc, 1);
+                    mma_tf32(acc, da, dw, idesc, 1);
                 }
                 mma_commit(empty(s));
+                mma_commit(lofree(b));
+                mma_commit(tfull(b));
             }
-            if (ok) mma_commit(accbar);
         }
-    } else if (warp >= 4) {
-        const int tid = threadIdx.x - 128;
+    } else if (warp < W_ACC0) {
+        const int tid = threadIdx.x - W_SPLIT0 * 32;
         for (int i = 0; i < nk && ok; ++i) {
-            const int s = i % G::STAGES;
-            const uint32_t ph = (i / G::STAGES) & 1;
-            if (!mbar_wait(full(s), ph, abort_flag)) { ok = false; break; }
-            split_tile(stageA(s), stageAlo(s), A_TILE, tid);
-            split_tile(stageW(s), stageWlo(s), G::W_TILE, tid);
+            const int s = i % S, b = i & 1;
+            if (!mbar_wait(full(s), (i / S) & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(lofree(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+            split_lo(stageA(s), bufAlo(b), A_TILE, tid, N_SPLIT * 32);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(conv(s));
         }
-        // epilogue: warp (w % 4) owns TMEM lanes 32*(w%4) .. +31 = tile rows
-        if (ok && mbar_wait(accbar, 0, abort_flag)) {
+    } else {
+        // accumulator / epilogue warps: warp w owns TMEM lanes 32*(w%4)..+31
+        // (tile rows) and one half of the tile's columns
+        constexpr int CPA = G::COLS_PER_ACC;
+        const int q = warp & 3, half = (warp - W_ACC0) >> 2;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + half * CPA;
+        float acc[CPA];
+#pragma unroll
+        for (int j = 0; j < CPA; ++j) acc[j] = 0.0f;
+        for (int i = 0; i < nk && ok; ++i) {
+            const int b = i & 1;
+            if (!mbar_wait(tfull(b), (i >> 1) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
-            const int q = warp & 3;
-            const int row = m0 + q * 32 + lane;
-            float *crow = C + (int64_t)row * ldc;
-#pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+#pragma unroll
+            for (int c = 0; c < CPA / 32; ++c) {
                 uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + ((uint32_t)(q * 32) << 16) + c0, r);
+                tmem_ld_32x32b_x32(lane_base + b * BN + c * 32, r);
                 tmem_ld_wait();
-                if (row < M) {
-                    const int nb = n0 + c0;
-                    float out[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        float v = __uint_as_float(r[j]);
-                        if (alpha != 1.0f) v = __fmul_rn(v, alpha);
-                        const int col = nb + j;
-                        if (bias && col < N) v = __fadd_rn(v, beta == 1.0f ? bias[col] : __fmul_rn(beta, bias[col]));
-                        if (epi == LONNX_EPI_RELU) v = v > 0.0f ? v : 0.0f;
-                        else if (epi == LONNX_EPI_GELU_ERF) v = lonnx_gelu_chain(v);
-                        out[j] = v;
-                    }
-                    if (nb + 32 <= N && (ldc & 3) == 0) {
+                for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __fadd_rn(acc[c * 32 + j], __uint_as_float(r[j]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tdrain(b));
+        }
+        const int row = m0 + q * 32 + lane;
+        if (ok && row < M) {
+            float *crow = C + (int64_t)row * ldc;
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4 *>(crow + nb + j) = make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]);
-                    } else {
-                        for (int j = 0; j < 32; ++j)
-                            if (nb + j < N) crow[nb + j] = out[j];
-                    }
+            for (int c = 0; c < CPA / 32; ++c) {
+                const int nb = n0 + half * CPA + c * 32;
+                float out[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    float v = acc[c * 32 + j];
+                    if (alpha != 1.0f) v = __fmul_rn(v, alpha);
+                    const int col = nb + j;
+                    if (bias && col < N) v = __fadd_rn(v, beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col)));
+                    if (epi == LONNX_EPI_RELU) v = v > 0.0f ? v : 0.0f;
+                    else if (epi == LONNX_EPI_GELU_ERF) v = lonnx_gelu_chain(v);
+                    out[j] = v;
+                }
+                if (nb + 32 <= N && (ldc & 3) == 0) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4 *>(crow + nb + j) = make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (nb + j < N) crow[nb + j] = out[j];
                 }
             }
-        } else {
-            ok = false;
         }
     }
 
@@ -214,19 +258,35 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     if (*abort_flag) {
         // drain before releasing TMEM / exiting: MMAs already issued, and TMA
         // loads that may still land in this CTA's shared memory (bounded waits)
-        if (warp == 1 && lane == 0) {
+        if (warp == W_MMA && lane == 0) {
             mma_commit(drainbar);
-            mbar_wait(drainbar, 0, nullptr, 200000000ull);
+            mbar_wait(drainbar, 0, nullptr, 400000000ll);
         }
-        if (warp == 0 && lane == 0) {
-            for (int j = issued - G::STAGES < 0 ? 0 : issued - G::STAGES; j < issued; ++j)
-                mbar_wait(full(j % G::STAGES), (j / G::STAGES) & 1, nullptr, 200000000ull);
+        if (warp == W_TMA && lane == 0) {
+            for (int j = issued - S < 0 ? 0 : issued - S; j < issued; ++j)
+                mbar_wait(full(j % S), (j / S) & 1, nullptr, 400000000ll);
         }
         __syncthreads();
     }
-    if (warp == 1) {
+    if (warp == W_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem, G::TMEM_COLS);
+    }
+}
+
+// Weight preparation: W given as [K, N] (trans = 0) or [N, K] (trans = 1)
+// -> hi, lo as [N, K] with hi = tf32(w) (low 13 mantissa bits cleared) and
+// lo = w - hi (exact).  Run once per weight; O(N K).
+__global__ void k_split_tf32_nk(const float *__restrict__ w, float *__restrict__ hi, float *__restrict__ lo,
+                                int K, int N, int trans) {
+    const int64_t n_el = (int64_t)N * K;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_el; i += stride) {
+        const int64_t nn = i / K, kk = i % K;
+        const float v = trans ? w[i] : w[kk * N + nn];
+        const float h = tf32_hi(v);
+        hi[i] = h;
+        lo[i] = __fsub_rn(v, h);
     }
 }
 
@@ -267,8 +327,8 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
 }
 
 template <int BN>
-int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, const float *bias,
-              float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi) {
+int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, const CUtensorMap &mwlo,
+              const float *bias, float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi) {
     using G = Cfg<BN>;
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {
@@ -276,35 +336,50 @@ int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, cons
         attr_set[ctx->device & 63] = true;
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-    k_gemm_tf32x3<BN><<<grid, kThreads, G::SMEM, ctx->stream>>>(ma, mw, bias, C, M, N, K, ldc, alpha, beta, epi,
+    k_gemm_tf32x3<BN><<<grid, kThreads, G::SMEM, ctx->stream>>>(ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi,
                                                                 ctx->dev_flags);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
+}
+
+// Tile width for N: 192 or 128, whichever divides N, else the one with the
+// least padding.
+int pick_bn(int N) {
+    if (N % 192 == 0) return 192;
+    if (N % 128 == 0) return 128;
+    return ((N + 191) / 192 * 192 - N) < ((N + 127) / 128 * 128 - N) ? 192 : 128;
 }
 
 }  // namespace
 
 namespace lonnx {
 
-int gemm_tc(lonnx_ctx *ctx, const float *A, const float *W, const float *bias,
-            const float *residual, float *C, int M, int N, int K, int lda, int ldw, int ldc,
-            float alpha, float beta, int epi) {
-    if (residual) return set_error(LONNX_E_UNSUPPORTED, "gemm_tc: residual epilogue not supported");
+int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, const float *bias, float *C, int M,
+            int N, int K, int lda, int ldw, int ldc, float alpha, float beta, int epi) {
     auto al16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
-    if (M <= 0 || N <= 0 || K <= 0 || (lda & 3) || (ldw & 3) || !al16(A) || !al16(W))
+    if (!Wlo) return set_error(LONNX_E_UNSUPPORTED, "gemm_tc: weight must be pre-split");
+    if (M <= 0 || N <= 0 || K <= 0 || (lda & 3) || (ldw & 3) || !al16(A) || !al16(Whi) || !al16(Wlo))
         return set_error(LONNX_E_UNSUPPORTED, "gemm_tc: operands not 16-byte aligned");
-    CUtensorMap ma, mw;
+    const int bn = pick_bn(N);
+    CUtensorMap ma, mw, mwlo;
     int rc = make_map(&ma, A, M, K, lda, BM);
     if (rc) return rc;
-    // Tile width: 128 columns unless N is large and a multiple of 256.
-    if (N >= 1024 && N % 256 == 0 && (int64_t)M * N >= (int64_t)148 * BM * 256) {
-        rc = make_map(&mw, W, N, K, ldw, 256);
-        if (rc) return rc;
-        return launch_tc<256>(ctx, ma, mw, bias, C, M, N, K, ldc, alpha, beta, epi);
-    }
-    rc = make_map(&mw, W, N, K, ldw, 128);
+    rc = make_map(&mw, Whi, N, K, ldw, bn);
     if (rc) return rc;
-    return launch_tc<128>(ctx, ma, mw, bias, C, M, N, K, ldc, alpha, beta, epi);
+    rc = make_map(&mwlo, Wlo, N, K, ldw, bn);
+    if (rc) return rc;
+    if (bn == 192) return launch_tc<192>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
+    return launch_tc<128>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
+}
+
+int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans) {
+    const int64_t n = (int64_t)N * K;
+    if (n <= 0) return LONNX_OK;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > (int64_t)ctx->num_sms * 16) blocks = (int64_t)ctx->num_sms * 16;
+    k_split_tf32_nk<<<(int)blocks, 256, 0, ctx->stream>>>(w, hi, lo, K, N, trans);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
 }
 
 }  // namespace lonnx

@@ -127,7 +127,8 @@ struct Step {
     std::vector<int> nodes;  // original node indices (fallback / S_NODE)
     // GEMM
     std::string x, y;        // input / output names
-    std::shared_ptr<DevBuf> wt;  // [N, K] weight
+    std::shared_ptr<DevBuf> wt;   // [N, K] weight, tf32 high parts
+    std::shared_ptr<DevBuf> wlo;  // [N, K] low parts (wt + wlo == W^T exactly)
     std::shared_ptr<DevBuf> bias;
     int N = 0, K = 0, epi = 0;
     std::vector<std::string> split_outputs;  // QKV: outputs per part (views), part width N/parts
@@ -820,8 +821,22 @@ bool exec_gemm_step(lonnx_graph *g, const Step &s) {
     std::vector<int64_t> oshape = xv.shape;
     oshape.back() = s.N;
     Value y = new_dev(g, DT_FLOAT, oshape);
-    ck(gemm_dispatch(g->ctx, (const float *)xv.dptr(), (const float *)s.wt->p, s.bias ? (const float *)s.bias->p : nullptr,
-                     (float *)y.dptr_mut(), 1, (int)M, s.N, s.K, 0, 0, 0, /*transB=*/1, 1.0f, 1.0f, s.epi, nullptr));
+    const float *bias = s.bias ? (const float *)s.bias->p : nullptr;
+    int rc = LONNX_E_UNSUPPORTED;
+    if ((int64_t)M * s.N * s.K >= gemm_tc_min_work() && s.K % 4 == 0)
+        rc = gemm_tc(g->ctx, (const float *)xv.dptr(), (const float *)s.wt->p, (const float *)s.wlo->p, bias,
+                     (float *)y.dptr_mut(), (int)M, s.N, s.K, s.K, s.K, s.N, 1.0f, 1.0f, s.epi);
+    if (rc == LONNX_E_UNSUPPORTED) {
+        // exact-order FFMA kernel on W^T = hi + lo (reassembled in scratch)
+        void *wfull = nullptr;
+        ck(ctx_scratch(g->ctx, (size_t)s.N * s.K * 4, &wfull));
+        const int64_t shp[1] = {(int64_t)s.N * s.K};
+        ck(lonnx_binary_f32(g->ctx, LONNX_ADD, (const float *)s.wt->p, shp, 1, (const float *)s.wlo->p, shp, 1,
+                            (float *)wfull));
+        rc = gemm_simt(g->ctx, (const float *)xv.dptr(), (const float *)wfull, bias, (float *)y.dptr_mut(), 1, (int)M,
+                       s.N, s.K, 0, 0, 0, 1, 1.0f, 1.0f, s.epi, nullptr);
+    }
+    ck(rc);
     g->env[s.y] = y;
     return true;
 }
@@ -1162,8 +1177,8 @@ void build_steps(lonnx_graph *g, bool fuse) {
         if (st.kind != S_GEMM) continue;
         const Value &W = g->inits.at(st.a);
         st.wt = std::make_shared<DevBuf>(g->ctx, (size_t)st.N * st.K * 4);
-        const int64_t shp[2] = {st.K, st.N}, perm[2] = {1, 0};
-        ck(transpose_launch(g->ctx, W.dptr(), 4, shp, 2, perm, st.wt->p));
+        st.wlo = std::make_shared<DevBuf>(g->ctx, (size_t)st.N * st.K * 4);
+        ck(split_tf32_nk(g->ctx, (const float *)W.dptr(), (float *)st.wt->p, (float *)st.wlo->p, st.K, st.N, 0));
         const Value &B = g->inits.at(st.b);
         st.bias = B.buf;
     }
@@ -1182,13 +1197,16 @@ void build_steps(lonnx_graph *g, bool fuse) {
         if (Q.x != Kq.x || Q.x != V.x || Q.K != Kq.K || Q.K != V.K || Q.N != Kq.N || Q.N != V.N) continue;
         const int H = Q.N, K = Q.K;
         auto wt = std::make_shared<DevBuf>(g->ctx, (size_t)3 * H * K * 4);
+        auto wlo = std::make_shared<DevBuf>(g->ctx, (size_t)3 * H * K * 4);
         auto bs = std::make_shared<DevBuf>(g->ctx, (size_t)3 * H * 4);
         Step *parts[3] = {&Q, &Kq, &V};
         for (int p = 0; p < 3; ++p) {
             ck(lonnx_memcpy_d2d(g->ctx, (float *)wt->p + (size_t)p * H * K, parts[p]->wt->p, (size_t)H * K * 4));
+            ck(lonnx_memcpy_d2d(g->ctx, (float *)wlo->p + (size_t)p * H * K, parts[p]->wlo->p, (size_t)H * K * 4));
             ck(lonnx_memcpy_d2d(g->ctx, (float *)bs->p + (size_t)p * H, parts[p]->bias->p, (size_t)H * 4));
         }
         Q.wt = wt;
+        Q.wlo = wlo;
         Q.bias = bs;
         Q.N = 3 * H;
         Q.y = "__qkv__" + at.y;

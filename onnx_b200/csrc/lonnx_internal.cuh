@@ -66,11 +66,16 @@ int device_guard(lonnx_ctx *ctx);
 int gemm_dispatch(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
                   int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
                   float alpha, float beta, int epi, const float *residual);
-// Tensor-core GEMM: C = A . W^T with W given K-major ([N, K] row-major);
-// returns LONNX_E_UNSUPPORTED when the shape does not fit its constraints.
-int gemm_tc(lonnx_ctx *ctx, const float *A, const float *W, const float *bias,
-            const float *residual, float *C, int M, int N, int K, int lda, int ldw, int ldc,
-            float alpha, float beta, int epi);
+// Tensor-core GEMM: C = A . W^T with the weight pre-split into Whi, Wlo,
+// both K-major ([N, K] row-major, see split_tf32_nk).  Returns
+// LONNX_E_UNSUPPORTED when the operands do not fit its constraints.
+int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, const float *bias,
+            float *C, int M, int N, int K, int lda, int ldw, int ldc, float alpha, float beta,
+            int epi);
+// Weight [K, N] (trans = 0) or [N, K] (trans = 1) -> hi, lo [N, K]:
+// hi = w with the low 13 mantissa bits cleared, lo = w - hi (exact).
+int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans);
+int64_t gemm_tc_min_work();
 int gemm_simt(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
               int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
               float alpha, float beta, int epi, const float *residual);

@@ -37,23 +37,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Wait for the phase of `parity` on `bar`, giving up after ~limit_ns or when
-// another thread of the CTA raised *abort.  Returns false on give-up.
+// Wait for the phase of `parity` on `bar`, giving up after ~limit_cycles SM
+// clocks (default ~2 s at 2 GHz) or when another thread of the CTA raised
+// *abort.  Returns false on give-up.  The timer is the SM's cycle counter
+// (clock64), which is cheap to read on the hand-off path.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort,
-                                          uint64_t limit_ns = 2000000000ull) {
+                                          long long limit_cycles = 4000000000ll) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
+    const long long t0 = clock64();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63) == 0) {
+        if ((it & 255) == 0) {
             if (abort && *abort) return false;
-            if (globaltimer_ns() - t0 > limit_ns) return false;
+            if (clock64() - t0 > limit_cycles) return false;
         }
     }
 }

@@ -130,3 +130,21 @@ def test_matmul_known_answer(ctx):
     r = P.MatMul(a, b)
     assert r.Status == "Success", r.Message
     assert r.Outputs[0][0, 1, 1] == 326.0
+
+
+def test_tf32_operand_truncation(ctx):
+    """The kernel uses the raw fp32 activation tile as the high part of the
+    split, relying on the tensor core reading an fp32 operand as its tf32
+    truncation.  Inputs whose low part is 3/4 of a tf32 ulp discriminate: a
+    rounding tensor core would take hi + 1 ulp and the result would be off by
+    ~1e-3 relative; truncation gives fp32 accuracy."""
+    rng = np.random.default_rng(12)
+    M, K, N = 512, 256, 512
+    base = rng.uniform(1, 2, (M, K)).astype(np.float32)
+    base = (base.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)  # tf32-exact
+    A = (base * np.float32(1 + 0.75 * 2.0 ** -10)).astype(np.float32)
+    B = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    ref = A.astype(np.float64) @ B.astype(np.float64)
+    got = _gemm(ctx, A, np.ascontiguousarray(B.T), transB=1)
+    rel = np.abs(got - ref).max() / np.abs(ref).max()
+    assert rel < 2e-6, rel
