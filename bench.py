@@ -1,0 +1,279 @@
+"""Benchmark: e5-small-shaped encoder inference on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+One step = one forward pass of the 12-layer encoder (hidden 384, 12 heads,
+FFN 1536, vocab 250037, seq 128) over a batch of B = 256 sequences per GPU,
+through the native graph executor (fused GEMM/attention/LayerNorm kernels).
+Multi-GPU is batch sharding with one full replica per GPU and no collective
+("weak" scaling: every rank runs B sequences); torch.distributed (NCCL) is
+used only for the start/stop barrier and the max-over-ranks timing.
+
+value: sequences/s with inputs already resident in HBM (CUDA events on the
+executor's stream).  e2e: the same through the public API with host numpy
+inputs -- H2D of the int64 ids/mask/type ids and D2H of the pooled
+embeddings inside the timed region.  roofline: the dominant kernel (the
+tensor-core GEMM at the FFN1 shape) timed live on its own.
+
+--impl reference times the reference's CPU algorithm on this host: the
+oracle's C restatement (oracle/, the reference itself is C#/.NET and cannot
+run here), one thread, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SEQ = 128
+METRIC = "e5-small encoder throughput (batch-sharded replicas)"
+UNIT = "seq/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    def __init__(self, gpu):
+        self.gpu = gpu
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits"],
+                                     capture_output=True, text=True, timeout=5).stdout.strip()
+                self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > i + 2 and "Active" in s[i + 2]
+                          and "Not" not in s[i + 2]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons}
+
+
+def build_graph(ctx, vocab):
+    from onnx_b200 import graphs as G
+    from onnx_b200.graph import ComputationalGraph
+    g = G.e5_encoder(vocab=vocab, seq=SEQ, seed=0)
+    g.outputs = ["sentence_embedding"]
+    return g, ComputationalGraph(g, ctx)
+
+
+def gemm_roofline(ctx, st, torch, M=32768, K=384, N=1536, reps=20):
+    """Live timing of the tensor-core GEMM kernel at the encoder's FFN1 shape
+    (weights pre-split, as in the graph), CUDA events on the launching stream."""
+    from onnx_b200 import _native as Nn
+    from onnx_b200.tensor import DeviceTensor
+    rng = np.random.default_rng(5)
+    A = DeviceTensor.from_host(ctx, rng.uniform(-1, 1, (M, K)).astype(np.float32))
+    W = DeviceTensor.from_host(ctx, rng.uniform(-1, 1, (N, K)).astype(np.float32))
+    C = DeviceTensor(ctx, (M, N), np.float32)
+    f = lambda: Nn.check(Nn.lib.lonnx_gemm_f32(ctx.handle, A.ptr, W.ptr, None, C.ptr, 1, M, N, K, 0, 0, 0, 1,
+                                               1.0, 1.0, 0))
+    for _ in range(3):
+        f()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        f()
+    e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps  # includes the O(NK) weight split launch of the generic entry point
+    _, bf16, kind = peaks()
+    tf32_peak = bf16 / 2.0
+    achieved = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    return {"bound": "tensor", "kernel": "k_gemm_tf32x3<192>", "shape": [M, K, N], "achieved": round(achieved, 2),
+            "peak": tf32_peak, "unit": "TFLOP/s", "frac": round(achieved / tf32_peak, 4),
+            "peak_note": f"dense tf32 = {kind} bf16 / 2; achieved counts algorithmic fp32 FLOPs (2MNK); "
+                         "3xTF32 issues 3 tf32 MMAs per product, so tensor-pipe use is 3x frac",
+            "traffic": None}
+
+
+def _oracle_graph():
+    from onnx_b200 import graphs as G
+    g = G.e5_encoder(vocab=250037, seq=SEQ, seed=0)
+    g.outputs = ["sentence_embedding"]
+    return g
+
+
+def cpu_baseline(n_seq=8, g=None):
+    """The oracle (C restatement of the reference's CPU ops, 1 thread) on a
+    bounded sample: n_seq full-length sequences through all 12 layers."""
+    from onnx_b200 import graphs as G
+    from oracle import oracle as O
+    g = g or _oracle_graph()
+    inp = G.e5_inputs(n_seq, SEQ, seed=0)
+    t0 = time.perf_counter()
+    O.execute(g, inp)
+    dt = time.perf_counter() - t0
+    return {"value": round(n_seq / dt, 4), "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"{n_seq} sequences x {SEQ} tokens, 12 layers, oracle/lonnx_oracle.c on 1 host thread "
+                      f"({dt:.2f} s); the reference itself is C#/.NET and no .NET runtime exists on this image"}
+
+
+def run_reference(args):
+    """Reference arm: the reference's CPU algorithm (oracle restatement) on the
+    host, rank 0 only; each step is a bounded 4-sequence sample."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    g = _oracle_graph()
+    for _ in range(min(args.warmup, 1)):
+        cpu_baseline(1, g)
+    vals = [cpu_baseline(4, g)["value"] for _ in range(args.steps)]
+    v = statistics.median(vals)
+    cb = {"value": v, "unit": UNIT, "cores": 1, "kind": "port",
+          "sample": "4 sequences x 128 tokens per step through the oracle (C restatement of Lokad.Onnx CPU ops, "
+                    "1 thread; the reference is single-threaded); the reference is C#/.NET and no .NET runtime "
+                    "exists on this image"}
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": "e5-small-shaped encoder (12 layers, hidden 384, 12 heads, "
+                                                        "FFN 1536, vocab 250037), seq 128, mean-pooled"},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=256, help="sequences per GPU")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--vocab", type=int, default=250037)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+
+    from onnx_b200 import graphs as G
+    from onnx_b200.tensor import Context, DeviceTensor
+    ctx = Context(local)
+    st = torch.cuda.ExternalStream(ctx.stream)
+    g, cg = build_graph(ctx, args.vocab)
+    B = args.batch
+    host_inp = G.e5_inputs(B, SEQ, args.vocab, seed=100 + rank)
+    dev_inp = {k: DeviceTensor.from_host(ctx, v) for k, v in host_inp.items()}
+    ctx.sync()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident (value) ----
+    cg.set_inputs(dev_inp)
+    for _ in range(args.warmup):
+        cg.run()
+    ctx.sync()
+    barrier()
+    torch.cuda.synchronize()
+    l0 = ctx.launches
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(st)
+        for _ in range(args.steps):
+            cg.run()
+        e1.record(st)
+        e1.synchronize()
+    ctx.sync()
+    launches = ctx.launches - l0  # all of this library's launches in the timed region
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    barrier()
+
+    # ---- end to end through the public API (host arrays in, host embeddings out) ----
+    for _ in range(args.warmup):
+        cg.execute(host_inp)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        out = cg.execute(host_inp)["sentence_embedding"]
+    ctx.sync()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / args.steps)
+    h2d = sum(v.nbytes for v in host_inp.values())
+    d2h = out.nbytes
+
+    roof = gemm_roofline(ctx, st, torch) if rank == 0 else None
+    clocks = clk.summary()
+    if rank == 0:
+        cb = None if args.no_cpu_baseline else cpu_baseline(8)
+        value = world * B / (ms * 1e-3)
+        line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32 (3xTF32 tensor-core GEMMs, fp32 accumulate)",
+                "data": "synthetic (seeded ids/masks, random-init N(0,0.02) weights)",
+                "config": {"workload": "e5-small-shaped encoder (12 layers, hidden 384, 12 heads, FFN 1536, "
+                                       "vocab 250037), seq 128, mean-pooled",
+                           "batch_per_gpu": B, "global_batch": B * world, "seq_len": SEQ,
+                           "parallelism": f"batch-sharded replicas x{world}, no collective",
+                           "l2": "working set per step >> 126 MB L2 (384 MB embedding table, 85 MB layer "
+                                 "weights, 50-200 MB activations); no explicit flush"},
+                "e2e": {"value": round(world * B / (e2e_ms * 1e-3), 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h},
+                "gpu_launches": launches * world, "gpu_launches_per_step_per_gpu": launches // args.steps, "roofline": roof, "cpu_baseline": cb, "clocks": clocks,
+                "flops_per_seq": G.e5_flops_per_seq()}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
