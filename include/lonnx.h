@@ -95,6 +95,19 @@ LONNX_API int lonnx_gemm_f32(lonnx_ctx *ctx, const float *A, const float *B, con
                              float *C, int batch, int M, int N, int K, int64_t strideA,
                              int64_t strideB, int64_t strideC, int transB, float alpha,
                              float beta, int epilogue);
+/* lonnx_gemm_f32 without any device allocation, for callers that cannot
+ * allocate device memory (a host callback or a plugin inside a runtime that
+ * owns the whole device pool, or code with no lonnx_ctx).  No counterpart in
+ * the reference.  Work goes on `stream` (a cudaStream_t) of the current
+ * device.  The tensor-core weight split uses a fixed 32 MiB file-scope device
+ * array, so N * K must be <= 4194304 (else LONNX_E_BADARG).  All calls on a
+ * device share that array: calls that overlap on the GPU race.  The first
+ * call on a device resolves the array's address; make it before any stream
+ * capture.  Expired device-side waits are not reported by this entry point. */
+LONNX_API int lonnx_gemm_f32_noalloc(void *stream, const float *A, const float *B, const float *bias,
+                                     float *C, int batch, int M, int N, int K, int64_t strideA,
+                                     int64_t strideB, int64_t strideC, int transB, float alpha,
+                                     float beta, int epilogue);
 /* ONNX MatMul with numpy batch broadcasting on the leading dimensions
  * (Tensor<float>.MatMul, TensorOps.cs:600-704).  y has shape
  * broadcast(a[:-2], b[:-2]) + [a[-2], b[-1]]. */

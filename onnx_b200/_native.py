@@ -40,6 +40,8 @@ _SIGS = {
     "lonnx_unary_f32": (c_int, [c_vp, c_int, c_vp, c_vp, c_i64]),
     "lonnx_gemm_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_i64,
                                c_i64, c_int, c_f32, c_f32, c_int]),
+    "lonnx_gemm_f32_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_i64,
+                                       c_i64, c_int, c_f32, c_f32, c_int]),
     "lonnx_matmul_f32": (c_int, [c_vp, c_vp, i64p, c_int, c_vp, i64p, c_int, c_vp]),
     "lonnx_conv2d_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp] + [c_int] * 17),
     "lonnx_softmax_f32": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64]),
