@@ -1,0 +1,42 @@
+"""Batch sharding across GPUs: one full graph replica per GPU, no collective
+on the data path.
+
+Every op of the encoder is independent across batch rows, so a batch is
+split into contiguous row slices (rank r gets rows [r*ceil(B/W), ...)), each
+rank runs its slice through its own replica, and the host concatenates the
+per-rank outputs in rank order.  torch.distributed is used only on the host
+(gather of the finished outputs) -- never inside the forward pass.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def shard_bounds(batch: int, world: int, rank: int):
+    per = -(-batch // world)
+    lo = min(rank * per, batch)
+    return lo, min(lo + per, batch)
+
+
+def shard_inputs(inputs: dict, world: int, rank: int) -> dict:
+    """Rows of every [B, ...] input that rank `rank` of `world` processes."""
+    b = next(iter(inputs.values())).shape[0]
+    lo, hi = shard_bounds(b, world, rank)
+    return {k: np.ascontiguousarray(v[lo:hi]) for k, v in inputs.items()}
+
+
+def gather_outputs(local: dict, group=None) -> dict:
+    """Concatenate each rank's host outputs in rank order (host-side gather)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    parts = [None] * world
+    dist.all_gather_object(parts, local, group=group)
+    return {k: np.concatenate([p[k] for p in parts], axis=0) for k in local}
+
+
+def run_sharded(execute, inputs: dict, group=None) -> dict:
+    """Run `execute(inputs_slice) -> dict` on this rank's slice and return the
+    full-batch outputs on every rank."""
+    import torch.distributed as dist
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    return gather_outputs(execute(shard_inputs(inputs, world, rank)), group)

@@ -10,6 +10,10 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (runs the CUDA library)")
+    # the library is built in-tree; build it when a checkout has none yet
+    if not os.path.exists(os.path.join(ROOT, "onnx_b200", "liblonnx_cuda.so")):
+        from onnx_b200 import build
+        build.build()
 
 
 @pytest.fixture(scope="session")
