@@ -105,7 +105,8 @@ extern "C" LONNX_API int lonnx_gemm_f32_noalloc(void *stream, const float *A, co
                 rc = split_tf32_nk(&c, B + b * strideB, hi, lo, K, N, transB);
                 if (rc) return rc;
             }
-            rc = gemm_tc(&c, A + b * strideA, hi, lo, bias, C + b * strideC, M, N, K, K, K, N, alpha, beta, epilogue);
+            rc = gemm_tc(&c, A + b * strideA, hi, lo, bias, C + b * strideC, M, N, K, K, K, N, alpha, beta, epilogue,
+                         /*allow_scratch=*/false);
             if (rc == LONNX_E_UNSUPPORTED && b == 0) break;
             if (rc) return rc;
             if (b == batch - 1) return LONNX_OK;

@@ -44,11 +44,12 @@ constexpr int kThreads = 384;           // 12 warps
 // warp roles: 0 TMA, 1 MMA + TMEM owner, 2-3 split A, 4-11 accumulate/epilogue
 constexpr int W_TMA = 0, W_MMA = 1, W_SPLIT0 = 2, N_SPLIT = 2, W_ACC0 = 4, N_ACC = 8;
 
-template <int BN>
+template <int BN, bool ALO>
 struct Cfg {
     static constexpr int W_TILE = BN * BK * 4;
-    static constexpr int STAGE = A_TILE + 2 * W_TILE;  // TMA ring: A, W_hi, W_lo
-    static constexpr int LO = 2 * A_TILE;              // A_lo ring: 2 buffers
+    // TMA ring: A, W_hi, W_lo (+ A_lo when it comes from HBM)
+    static constexpr int STAGE = (ALO ? 2 : 1) * A_TILE + 2 * W_TILE;
+    static constexpr int LO = ALO ? 0 : 2 * A_TILE;    // in-kernel A_lo ring: 2 buffers
     static constexpr int STAGES = (4 * STAGE + LO + 1280 <= 227 * 1024) ? 4
                                   : (3 * STAGE + LO + 1280 <= 227 * 1024) ? 3 : 2;
     static constexpr int SMEM = STAGES * STAGE + LO + 1024 /*align*/ + 256 /*barriers*/;
@@ -85,12 +86,13 @@ __device__ __forceinline__ void split_lo(const uint8_t *buf, uint8_t *lo_buf, in
 // reads of three MMAs + TMA writes + the split), which is why the weight is
 // split once ahead of time and A_lo has its own 2-buffer ring (so the TMA
 // ring can be 3-4 stages deep).
-template <int BN>
+template <int BN, bool ALO>
 __global__ void __launch_bounds__(kThreads, 1)
-k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-              const __grid_constant__ CUtensorMap tmWlo, const float *__restrict__ bias, float *__restrict__ C,
-              int M, int N, int K, int ldc, float alpha, float beta, int epi, int *dev_flags) {
-    using G = Cfg<BN>;
+k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAlo,
+              const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmWlo,
+              const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, int ldc, float alpha,
+              float beta, int epi, int *dev_flags) {
+    using G = Cfg<BN, ALO>;
     constexpr int S = G::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -114,13 +116,14 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     auto stageA = [&](int s) { return smem + s * G::STAGE; };
     auto stageW = [&](int s) { return smem + s * G::STAGE + A_TILE; };
     auto stageWlo = [&](int s) { return smem + s * G::STAGE + A_TILE + G::W_TILE; };
+    auto stageAlo = [&](int s) { return smem + s * G::STAGE + A_TILE + 2 * G::W_TILE; };
     auto bufAlo = [&](int b) { return smem + S * G::STAGE + b * A_TILE; };
     int issued = 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full(s), 1);
-            mbar_init(conv(s), N_SPLIT);
+            mbar_init(conv(s), ALO ? 1 : N_SPLIT);
             mbar_init(empty(s), 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -134,6 +137,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmW);
         prefetch_tmap(&tmWlo);
+        if (ALO) prefetch_tmap(&tmAlo);
     }
     if (warp == W_MMA) {
         tmem_alloc(smem_u32(tmem_slot), G::TMEM_COLS);
@@ -147,7 +151,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
 
     if (warp == W_TMA) {
         if (lane == 0) {
-            constexpr uint32_t bytes = A_TILE + 2 * G::W_TILE;
+            constexpr uint32_t bytes = G::STAGE;
             for (int i = 0; i < nk && ok; ++i) {
                 const int s = i % S;
                 if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -155,6 +159,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), i * BK, m0);
                 tma_load_2d(smem_u32(stageW(s)), &tmW, full(s), i * BK, n0);
                 tma_load_2d(smem_u32(stageWlo(s)), &tmWlo, full(s), i * BK, n0);
+                if (ALO) tma_load_2d(smem_u32(stageAlo(s)), &tmAlo, full(s), i * BK, m0);
                 issued = i + 1;
             }
         }
@@ -163,11 +168,11 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             constexpr uint32_t idesc = idesc_tf32(BM, BN);
             for (int i = 0; i < nk && ok; ++i) {
                 const int s = i % S, b = i & 1;
-                if (!mbar_wait(conv(s), (i / S) & 1, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(ALO ? full(s) : conv(s), (i / S) & 1, abort_flag)) { ok = false; break; }
                 if (!mbar_wait(tdrain(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t acc = tmem + b * BN;
-                const uint32_t a = smem_u32(stageA(s)), alo = smem_u32(bufAlo(b));
+                const uint32_t a = smem_u32(stageA(s)), alo = smem_u32(ALO ? stageAlo(s) : bufAlo(b));
                 const uint32_t w = smem_u32(stageW(s)), wlo = smem_u32(stageWlo(s));
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
@@ -184,6 +189,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             }
         }
     } else if (warp < W_ACC0) {
+        if (ALO) goto done_roles;
         const int tid = threadIdx.x - W_SPLIT0 * 32;
         for (int i = 0; i < nk && ok; ++i) {
             const int s = i % S, b = i & 1;
@@ -219,36 +225,56 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             __syncwarp();
             if (lane == 0) mbar_arrive(tdrain(b));
         }
-        const int row = m0 + q * 32 + lane;
-        if (ok && row < M) {
-            float *crow = C + (int64_t)row * ldc;
+        // epilogue: raw sums staged row-major in the (now idle) stage buffers,
+        // then one pass that applies alpha, bias and the activation and writes
+        // coalesced 16-byte stores.  The activation code appears once (a
+        // per-element unrolled epilogue with Erf-GELU inlined overflows the
+        // instruction cache).
+        constexpr int PITCH = BN + 4;  // floats; keeps the per-row writes conflict-free
+        static_assert(BM * PITCH * 4 <= G::STAGES * G::STAGE, "C tile must fit in the stage ring");
+        float *ctile = reinterpret_cast<float *>(smem);
+        const int rloc = q * 32 + lane;
+        if (ok) {
 #pragma unroll
-            for (int c = 0; c < CPA / 32; ++c) {
-                const int nb = n0 + half * CPA + c * 32;
-                float out[32];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    float v = acc[c * 32 + j];
-                    if (alpha != 1.0f) v = __fmul_rn(v, alpha);
-                    const int col = nb + j;
-                    if (bias && col < N) v = __fadd_rn(v, beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col)));
-                    if (epi == LONNX_EPI_RELU) v = v > 0.0f ? v : 0.0f;
-                    else if (epi == LONNX_EPI_GELU_ERF) v = lonnx_gelu_chain(v);
-                    out[j] = v;
+            for (int j = 0; j < CPA; j += 4)
+                *reinterpret_cast<float4 *>(ctile + rloc * PITCH + half * CPA + j) =
+                    make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(N_ACC * 32) : "memory");
+        if (ok) {
+            const int t = threadIdx.x - W_ACC0 * 32;
+            constexpr int V4 = BN / 4;  // float4 per tile row
+            const bool vec = (ldc & 3) == 0 && n0 + BN <= N;
+#pragma unroll 1
+            for (int e = t; e < BM * V4; e += N_ACC * 32) {
+                const int r = e / V4, c4 = e % V4;
+                const int grow = m0 + r;
+                if (grow >= M) continue;
+                const float4 raw = *reinterpret_cast<const float4 *>(ctile + r * PITCH + c4 * 4);
+                float v[4] = {raw.x, raw.y, raw.z, raw.w};
+                const int col0 = n0 + c4 * 4;
+#pragma unroll 1
+                for (int u = 0; u < 4; ++u) {
+                    float x = v[u];
+                    if (alpha != 1.0f) x = __fmul_rn(x, alpha);
+                    if (bias && col0 + u < N)
+                        x = __fadd_rn(x, beta == 1.0f ? __ldg(bias + col0 + u) : __fmul_rn(beta, __ldg(bias + col0 + u)));
+                    if (epi == LONNX_EPI_RELU) x = x > 0.0f ? x : 0.0f;
+                    else if (epi == LONNX_EPI_GELU_ERF) x = lonnx_gelu_chain(x);
+                    v[u] = x;
                 }
-                if (nb + 32 <= N && (ldc & 3) == 0) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        *reinterpret_cast<float4 *>(crow + nb + j) = make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]);
+                float *dst = C + (int64_t)grow * ldc + col0;
+                if (vec) {
+                    *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
                 } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (nb + j < N) crow[nb + j] = out[j];
+                    for (int u = 0; u < 4; ++u)
+                        if (col0 + u < N) dst[u] = v[u];
                 }
             }
         }
     }
 
+done_roles:
     if (!ok) {
         *abort_flag = 1;
         atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
@@ -271,6 +297,16 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     if (warp == W_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem, G::TMEM_COLS);
+    }
+}
+
+// Activation low parts: lo = a - tf32(a), row-major like a (fp32 streaming).
+__global__ void k_split_lo(const float4 *__restrict__ a, float4 *__restrict__ lo, int64_t n4) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const float4 v = __ldg(a + i);
+        lo[i] = make_float4(__fsub_rn(v.x, tf32_hi(v.x)), __fsub_rn(v.y, tf32_hi(v.y)), __fsub_rn(v.z, tf32_hi(v.z)),
+                            __fsub_rn(v.w, tf32_hi(v.w)));
     }
 }
 
@@ -326,18 +362,19 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
     return LONNX_OK;
 }
 
-template <int BN>
-int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, const CUtensorMap &mwlo,
-              const float *bias, float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi) {
-    using G = Cfg<BN>;
+template <int BN, bool ALO>
+int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &malo, const CUtensorMap &mw,
+              const CUtensorMap &mwlo, const float *bias, float *C, int M, int N, int K, int ldc, float alpha,
+              float beta, int epi) {
+    using G = Cfg<BN, ALO>;
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {
-        LONNX_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
+        LONNX_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, ALO>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
         attr_set[ctx->device & 63] = true;
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-    k_gemm_tf32x3<BN><<<grid, kThreads, G::SMEM, ctx->stream>>>(ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi,
-                                                                ctx->dev_flags);
+    k_gemm_tf32x3<BN, ALO><<<grid, kThreads, G::SMEM, ctx->stream>>>(ma, malo, mw, mwlo, bias, C, M, N, K, ldc, alpha,
+                                                                     beta, epi, ctx->dev_flags);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
 }
@@ -355,7 +392,7 @@ int pick_bn(int N) {
 namespace lonnx {
 
 int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, const float *bias, float *C, int M,
-            int N, int K, int lda, int ldw, int ldc, float alpha, float beta, int epi) {
+            int N, int K, int lda, int ldw, int ldc, float alpha, float beta, int epi, bool allow_scratch) {
     auto al16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
     if (!Wlo) return set_error(LONNX_E_UNSUPPORTED, "gemm_tc: weight must be pre-split");
     if (M <= 0 || N <= 0 || K <= 0 || (lda & 3) || (ldw & 3) || !al16(A) || !al16(Whi) || !al16(Wlo))
@@ -368,8 +405,32 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
     if (rc) return rc;
     rc = make_map(&mwlo, Wlo, N, K, ldw, bn);
     if (rc) return rc;
-    if (bn == 192) return launch_tc<192>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
-    return launch_tc<128>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
+    // A's low parts: split inside the kernel per tile (default), or streamed
+    // once into scratch and TMA-loaded beside A when many N tiles would each
+    // repeat the split (N >= 3072).  LONNX_GEMM_ALO=0/1 forces either.
+    static const int mode = [] {
+        const char *e = getenv("LONNX_GEMM_ALO");
+        return e ? atoi(e) : -1;
+    }();
+    const bool alo = mode < 0 ? N >= 3072 : mode != 0;
+    if (alo && allow_scratch) {
+        // A_lo streamed into scratch, then TMA-loaded beside A
+        void *tmp = nullptr;
+        rc = ctx_scratch2(ctx, (size_t)M * lda * 4, &tmp);
+        if (rc) return rc;
+        const int64_t n4 = (int64_t)M * lda / 4;
+        int64_t blocks = (n4 + 255) / 256;
+        if (blocks > (int64_t)ctx->num_sms * 16) blocks = (int64_t)ctx->num_sms * 16;
+        k_split_lo<<<(int)blocks, 256, 0, ctx->stream>>>((const float4 *)A, (float4 *)tmp, n4);
+        LONNX_CHECK_LAUNCH(ctx);
+        CUtensorMap malo;
+        rc = make_map(&malo, (const float *)tmp, M, K, lda, BM);
+        if (rc) return rc;
+        if (bn == 192) return launch_tc<192, true>(ctx, ma, malo, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
+        return launch_tc<128, true>(ctx, ma, malo, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
+    }
+    if (bn == 192) return launch_tc<192, false>(ctx, ma, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
+    return launch_tc<128, false>(ctx, ma, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
 }
 
 int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans) {

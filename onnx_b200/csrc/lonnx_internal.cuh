@@ -39,6 +39,8 @@ struct lonnx_ctx {
     // operand of a tensor-core GEMM); grown on demand, owned by the context
     void *scratch = nullptr;
     size_t scratch_bytes = 0;
+    void *scratch2 = nullptr;
+    size_t scratch2_bytes = 0;
 };
 
 namespace lonnx {
@@ -60,6 +62,8 @@ int cuda_error(cudaError_t e, const char *what);
 int ctx_alloc(lonnx_ctx *ctx, size_t bytes, void **out);
 int ctx_free(lonnx_ctx *ctx, void *p);
 int ctx_scratch(lonnx_ctx *ctx, size_t bytes, void **out);
+// second, independent scratch slot (the GEMM's activation low parts)
+int ctx_scratch2(lonnx_ctx *ctx, size_t bytes, void **out);
 int device_guard(lonnx_ctx *ctx);
 
 // kernels implemented in other translation units (device pointers, ctx stream)
@@ -69,9 +73,11 @@ int gemm_dispatch(lonnx_ctx *ctx, const float *A, const float *B, const float *b
 // Tensor-core GEMM: C = A . W^T with the weight pre-split into Whi, Wlo,
 // both K-major ([N, K] row-major, see split_tf32_nk).  Returns
 // LONNX_E_UNSUPPORTED when the operands do not fit its constraints.
+// allow_scratch = false keeps the call free of device allocation (the
+// activation split then happens inside the kernel).
 int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, const float *bias,
             float *C, int M, int N, int K, int lda, int ldw, int ldc, float alpha, float beta,
-            int epi);
+            int epi, bool allow_scratch = true);
 // Weight [K, N] (trans = 0) or [N, K] (trans = 1) -> hi, lo [N, K]:
 // hi = w with the low 13 mantissa bits cleared, lo = w - hi (exact).
 int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans);

@@ -103,6 +103,22 @@ int ctx_scratch(lonnx_ctx *ctx, size_t bytes, void **out) {
     return LONNX_OK;
 }
 
+int ctx_scratch2(lonnx_ctx *ctx, size_t bytes, void **out) {
+    if (bytes > ctx->scratch2_bytes) {
+        if (ctx->scratch2) {
+            LONNX_CUDA(cudaStreamSynchronize(ctx->stream));
+            ctx_free(ctx, ctx->scratch2);
+            ctx->scratch2 = nullptr;
+            ctx->scratch2_bytes = 0;
+        }
+        int rc = ctx_alloc(ctx, bytes, &ctx->scratch2);
+        if (rc) return rc;
+        ctx->scratch2_bytes = bytes;
+    }
+    *out = ctx->scratch2;
+    return LONNX_OK;
+}
+
 }  // namespace lonnx
 
 using namespace lonnx;
