@@ -123,7 +123,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full(s), 1);
-            mbar_init(conv(s), ALO ? 1 : N_SPLIT);
+            mbar_init(conv(s), ALO ? 1 : N_SPLIT + N_ACC);
             mbar_init(empty(s), 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -195,7 +195,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             const int s = i % S, b = i & 1;
             if (!mbar_wait(full(s), (i / S) & 1, abort_flag)) { ok = false; break; }
             if (!mbar_wait(lofree(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
-            split_lo(stageA(s), bufAlo(b), A_TILE, tid, N_SPLIT * 32);
+            split_lo(stageA(s), bufAlo(b), A_TILE, tid, (N_SPLIT + N_ACC) * 32);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(conv(s));
@@ -209,9 +209,13 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         float acc[CPA];
 #pragma unroll
         for (int j = 0; j < CPA; ++j) acc[j] = 0.0f;
-        for (int i = 0; i < nk && ok; ++i) {
+        // per iteration: help split stage i (unless A_lo comes from HBM), then
+        // drain chunk i-1 -- the drain of a chunk never waits on a split the
+        // same warps still have to do
+        const int stid = N_SPLIT * 32 + (threadIdx.x - W_ACC0 * 32);
+        auto drain = [&](int i) {
             const int b = i & 1;
-            if (!mbar_wait(tfull(b), (i >> 1) & 1, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(tfull(b), (i >> 1) & 1, abort_flag)) return false;
             tc_fence_after();
 #pragma unroll
             for (int c = 0; c < CPA / 32; ++c) {
@@ -224,6 +228,19 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tdrain(b));
+            return true;
+        };
+        for (int i = 0; i <= nk && ok; ++i) {
+            if (!ALO && i < nk) {
+                const int s = i % S, b = i & 1;
+                if (!mbar_wait(full(s), (i / S) & 1, abort_flag) ||
+                    !mbar_wait(lofree(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                split_lo(stageA(s), bufAlo(b), A_TILE, stid, (N_SPLIT + N_ACC) * 32);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(conv(s));
+            }
+            if (i > 0 && !drain(i - 1)) { ok = false; break; }
         }
         // epilogue: raw sums staged row-major in the (now idle) stage buffers,
         // then one pass that applies alpha, bias and the activation and writes
@@ -233,7 +250,18 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         constexpr int PITCH = BN + 4;  // floats; keeps the per-row writes conflict-free
         static_assert(BM * PITCH * 4 <= G::STAGES * G::STAGE, "C tile must fit in the stage ring");
         float *ctile = reinterpret_cast<float *>(smem);
+        float *sbias = ctile + BM * PITCH;  // BN floats
+        static_assert(BM * PITCH * 4 + BN * 4 <= G::STAGES * G::STAGE, "C tile + bias must fit in the stage ring");
         const int rloc = q * 32 + lane;
+        {
+            const int t = threadIdx.x - W_ACC0 * 32;
+            for (int c = t; c < BN; c += N_ACC * 32) {
+                const int col = n0 + c;
+                float bv = 0.0f;
+                if (bias && col < N) bv = beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col));
+                sbias[c] = bv;
+            }
+        }
         if (ok) {
 #pragma unroll
             for (int j = 0; j < CPA; j += 4)
@@ -253,12 +281,11 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 const float4 raw = *reinterpret_cast<const float4 *>(ctile + r * PITCH + c4 * 4);
                 float v[4] = {raw.x, raw.y, raw.z, raw.w};
                 const int col0 = n0 + c4 * 4;
-#pragma unroll 1
+#pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     float x = v[u];
                     if (alpha != 1.0f) x = __fmul_rn(x, alpha);
-                    if (bias && col0 + u < N)
-                        x = __fadd_rn(x, beta == 1.0f ? __ldg(bias + col0 + u) : __fmul_rn(beta, __ldg(bias + col0 + u)));
+                    if (bias) x = __fadd_rn(x, sbias[c4 * 4 + u]);
                     if (epi == LONNX_EPI_RELU) x = x > 0.0f ? x : 0.0f;
                     else if (epi == LONNX_EPI_GELU_ERF) x = lonnx_gelu_chain(x);
                     v[u] = x;
