@@ -13,6 +13,8 @@
 // rounding: score = (q.k) / scale + mask; softmax with the running max
 // starting at 0 (the reference ReduceMax, TensorOps.cs:1820); sequential
 // sums over keys, as the reference's i-j-k matmul accumulates.
+#include <stdlib.h>
+
 #include "lonnx_internal.cuh"
 
 namespace {
@@ -96,14 +98,116 @@ k_attention(const float *__restrict__ q, const float *__restrict__ k, const floa
     for (int d = 0; d < DH; d += 4) *reinterpret_cast<float4 *>(op + d) = make_float4(acc[d], acc[d + 1], acc[d + 2], acc[d + 3]);
 }
 
+// Online-softmax variant: scores stay in registers, 32 keys at a time; the
+// running max starts at 0 like the reference's ReduceMax (shift-invariant),
+// exp-sums and the P.V accumulation are rescaled when the max grows, and the
+// division by the row sum happens once at the end.  FMA contractions; the
+// result matches the node chain within fp32 rounding.
+template <int DH>
+__global__ void __launch_bounds__(QT)
+k_attention_online(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+                   int64_t ld, const float *__restrict__ maskadd, float *__restrict__ out, int S, int heads,
+                   float scale) {
+    extern __shared__ float sm[];
+    float *Ks = sm;                   // [S][DH]
+    float *Vs = Ks + (size_t)S * DH;  // [S][DH]
+    float *Ms = Vs + (size_t)S * DH;  // [S] additive mask
+    const int bh = blockIdx.y;
+    const int b = bh / heads, h = bh % heads;
+    const int tid = threadIdx.x;
+    const int64_t base = (int64_t)b * S * ld + (int64_t)h * DH;
+    for (int e = tid; e < S * DH / 4; e += QT) {
+        const int r = e / (DH / 4), c = (e % (DH / 4)) * 4;
+        *reinterpret_cast<float4 *>(Ks + r * DH + c) = __ldg(reinterpret_cast<const float4 *>(k + base + (int64_t)r * ld + c));
+        *reinterpret_cast<float4 *>(Vs + r * DH + c) = __ldg(reinterpret_cast<const float4 *>(v + base + (int64_t)r * ld + c));
+    }
+    for (int j = tid; j < S; j += QT) Ms[j] = maskadd ? maskadd[(int64_t)b * S + j] : 0.0f;
+    __syncthreads();
+    const int i = blockIdx.x * QT + tid;
+    if (i >= S) return;
+    const float inv_scale = 1.0f / scale;
+    float qr[DH];
+    const float *qp = q + base + (int64_t)i * ld;
+#pragma unroll
+    for (int d = 0; d < DH; d += 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4 *>(qp + d));
+        qr[d] = t.x * inv_scale; qr[d + 1] = t.y * inv_scale; qr[d + 2] = t.z * inv_scale; qr[d + 3] = t.w * inv_scale;
+    }
+    float acc[DH];
+#pragma unroll
+    for (int d = 0; d < DH; ++d) acc[d] = 0.0f;
+    float m = 0.0f, l = 0.0f;
+    constexpr int KC = 32;
+    for (int j0 = 0; j0 < S; j0 += KC) {
+        float sc[KC];
+        float cmax = m;
+#pragma unroll
+        for (int jj = 0; jj < KC; ++jj) {
+            const int j = j0 + jj;
+            float dot = -INFINITY;
+            if (j < S) {
+                const float *kr = Ks + j * DH;
+                dot = 0.0f;
+#pragma unroll
+                for (int d = 0; d < DH; d += 4) {
+                    const float4 kk = *reinterpret_cast<const float4 *>(kr + d);
+                    dot = fmaf(qr[d], kk.x, dot);
+                    dot = fmaf(qr[d + 1], kk.y, dot);
+                    dot = fmaf(qr[d + 2], kk.z, dot);
+                    dot = fmaf(qr[d + 3], kk.w, dot);
+                }
+                dot += Ms[j];
+            }
+            sc[jj] = dot;
+            cmax = fmaxf(cmax, dot);
+        }
+        const float corr = expf(m - cmax);
+        m = cmax;
+        l *= corr;
+#pragma unroll
+        for (int d = 0; d < DH; ++d) acc[d] *= corr;
+#pragma unroll
+        for (int jj = 0; jj < KC; ++jj) {
+            const int j = j0 + jj;
+            if (j >= S) break;
+            const float p = expf(sc[jj] - m);
+            l += p;
+            const float *vr = Vs + j * DH;
+#pragma unroll
+            for (int d = 0; d < DH; d += 4) {
+                const float4 vv = *reinterpret_cast<const float4 *>(vr + d);
+                acc[d] = fmaf(p, vv.x, acc[d]);
+                acc[d + 1] = fmaf(p, vv.y, acc[d + 1]);
+                acc[d + 2] = fmaf(p, vv.z, acc[d + 2]);
+                acc[d + 3] = fmaf(p, vv.w, acc[d + 3]);
+            }
+        }
+    }
+    const float inv_l = 1.0f / l;
+    float *op = out + ((int64_t)b * S + i) * ((int64_t)heads * DH) + (int64_t)h * DH;
+#pragma unroll
+    for (int d = 0; d < DH; d += 4)
+        *reinterpret_cast<float4 *>(op + d) = make_float4(acc[d] * inv_l, acc[d + 1] * inv_l, acc[d + 2] * inv_l, acc[d + 3] * inv_l);
+}
+
 template <int DH>
 int launch_attn(lonnx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld,
                 const float *mask, float *out, int B, int S, int heads, float scale) {
+    static const bool exact = getenv("LONNX_ATTN_EXACT") != nullptr;
+    dim3 grid((S + QT - 1) / QT, B * heads);
+    if (!exact) {
+        const size_t smem = ((size_t)2 * S * DH + S) * sizeof(float);
+        if (smem <= 227 * 1024) {
+            LONNX_CUDA(cudaFuncSetAttribute(k_attention_online<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            k_attention_online<DH><<<grid, QT, smem, ctx->stream>>>(q, k, v, ld, mask, out, S, heads, scale);
+            LONNX_CHECK_LAUNCH(ctx);
+            return LONNX_OK;
+        }
+    }
     const size_t smem = ((size_t)2 * S * DH + (size_t)QT * (S + 1)) * sizeof(float);
     if (smem > 227 * 1024)
         return lonnx::set_error(LONNX_E_UNSUPPORTED, "attention: sequence length %d too long for the fused kernel", S);
     LONNX_CUDA(cudaFuncSetAttribute(k_attention<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid((S + QT - 1) / QT, B * heads);
     k_attention<DH><<<grid, QT, smem, ctx->stream>>>(q, k, v, ld, mask, out, S, heads, scale);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
