@@ -174,6 +174,45 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def profile_case(batch):
+    """A small, fast workload of the same kernels for profiler captures."""
+    from onnx_b200 import graphs as G
+    from onnx_b200.graph import ComputationalGraph
+    from onnx_b200.tensor import Context
+    ctx = Context(0)
+    g = G.e5_encoder(layers=2, vocab=30000, seq=SEQ, seed=0)
+    g.outputs = ["sentence_embedding"]
+    cg = ComputationalGraph(g, ctx)
+    inp = G.e5_inputs(batch, SEQ, 30000)
+    for _ in range(2):
+        cg.execute(inp)
+    print("profile case done")
+
+
+def mnist_latency(ctx, st, torch, reps=200):
+    """MNIST-8 CNN at batch 1: device-resident input,
+    CUDA-event time per forward and the img/s it implies."""
+    from onnx_b200 import graphs as G
+    from onnx_b200.graph import ComputationalGraph
+    from onnx_b200.tensor import DeviceTensor
+    g = G.mnist8(seed=0)
+    cg = ComputationalGraph(g, ctx)
+    x = DeviceTensor.from_host(ctx, np.random.default_rng(0).uniform(0, 1, (1, 1, 28, 28)).astype(np.float32))
+    cg.set_inputs({"Input3": x})
+    for _ in range(10):
+        cg.run()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        cg.run()
+    e1.record(st)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / reps
+    return {"metric": "MNIST-8 CNN img/s at batch 1 (device-resident input)", "img_per_s": round(1e6 / us, 1),
+            "us_per_img": round(us, 2), "flops_per_img": 1573120}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -183,7 +222,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--vocab", type=int, default=250037)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", type=int, default=0, metavar="B",
+                    help="run two 2-layer e5 forwards at batch B and exit (small case for ncu captures)")
     args = ap.parse_args()
+    if args.profile_case:
+        return profile_case(args.profile_case)
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
@@ -252,6 +295,7 @@ def main():
     d2h = out.nbytes
 
     roof = gemm_roofline(ctx, st, torch) if rank == 0 else None
+    mnist = mnist_latency(ctx, st, torch) if rank == 0 else None
     clocks = clk.summary()
     if rank == 0:
         cb = None if args.no_cpu_baseline else cpu_baseline(8)
@@ -269,7 +313,7 @@ def main():
                 "e2e": {"value": round(world * B / (e2e_ms * 1e-3), 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches * world, "gpu_launches_per_step_per_gpu": launches // args.steps, "roofline": roof, "cpu_baseline": cb, "clocks": clocks,
-                "flops_per_seq": G.e5_flops_per_seq()}
+                "flops_per_seq": G.e5_flops_per_seq(), "mnist": mnist}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
