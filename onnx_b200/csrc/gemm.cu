@@ -123,6 +123,44 @@ __global__ void k_conv2d_direct(const float *__restrict__ x, const float *__rest
     }
 }
 
+// im2col in row-per-output-pixel form for the tensor-core conv:
+// col[(n, oy, ox), k] with k = (c, ky, kx) in the reference's im2col row order
+// (MathOps.cs:654-709), K padded with zeros to ldk (a multiple of 4, for TMA).
+__global__ void k_im2col_rows(const float *__restrict__ x, float *__restrict__ col, int N, int C, int H, int W,
+                              int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw, int Ho, int Wo, int K,
+                              int ldk) {
+    const int64_t total = (int64_t)N * Ho * Wo * ldk;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += stride) {
+        const int k = (int)(t % ldk);
+        const int64_t pix = t / ldk;
+        float v = 0.0f;
+        if (k < K) {
+            const int ox = (int)(pix % Wo), oy = (int)((pix / Wo) % Ho);
+            const int n = (int)(pix / ((int64_t)Wo * Ho));
+            const int kx = k % kw, ky = (k / kw) % kh, c = k / (kw * kh);
+            const int iy = oy * sh - pt + ky * dh, ix = ox * sw - pl + kx * dw;
+            if (iy >= 0 && iy < H && ix >= 0 && ix < W) v = __ldg(x + (((int64_t)n * C + c) * H + iy) * W + ix);
+        }
+        col[t] = v;
+    }
+}
+
+// weight [M, K] -> hi, lo [M, ldk] (tf32 split, zero padded)
+__global__ void k_split_pad_rows(const float *__restrict__ w, float *__restrict__ hi, float *__restrict__ lo, int M,
+                                 int K, int ldk) {
+    const int64_t total = (int64_t)M * ldk;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += stride) {
+        const int k = (int)(t % ldk);
+        const int64_t m = t / ldk;
+        const float v = k < K ? w[m * K + k] : 0.0f;
+        const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+        hi[t] = h;
+        lo[t] = __fsub_rn(v, h);
+    }
+}
+
 inline int grid_for(lonnx_ctx *ctx, int64_t work, int threads = 256) {
     int64_t blocks = (work + threads - 1) / threads;
     const int64_t cap = (int64_t)ctx->num_sms * 16;
@@ -301,6 +339,39 @@ LONNX_API int lonnx_conv2d_f32(lonnx_ctx *ctx, const float *x, const float *w, c
     if (Ho <= 0 || Wo <= 0) return set_error(LONNX_E_SHAPE, "conv2d: empty output");
     const int64_t total = (int64_t)N * M * Ho * Wo;
     if (total == 0) return LONNX_OK;
+    const int K = C * kh * kw;
+    static const bool tc_off = getenv("LONNX_DISABLE_TC") != nullptr;
+    if (!tc_off && group == 1 && total * K >= gemm_tc_min_work()) {
+        // GEMM formulation on the tensor cores: rows = output pixels (N*Ho*Wo),
+        // cols = output channels, contraction over (c, ky, kx); per-channel
+        // bias and ReLU in the GEMM epilogue; NHWC result -> NCHW.
+        const int ldk = (K + 3) & ~3;
+        const int64_t P = (int64_t)N * Ho * Wo;
+        void *col = nullptr, *wt = nullptr, *tmp = nullptr;
+        rc = ctx_alloc(ctx, (size_t)P * ldk * 4, &col);
+        if (rc) return rc;
+        rc = ctx_alloc(ctx, (size_t)2 * M * ldk * 4, &wt);
+        if (rc) { ctx_free(ctx, col); return rc; }
+        rc = ctx_alloc(ctx, (size_t)P * M * 4, &tmp);
+        if (rc) { ctx_free(ctx, col); ctx_free(ctx, wt); return rc; }
+        k_im2col_rows<<<grid_for(ctx, P * ldk), 256, 0, ctx->stream>>>(x, (float *)col, N, C, H, W, kh, kw, sh, sw, pt,
+                                                                       pl, dh, dw, Ho, Wo, K, ldk);
+        LONNX_CHECK_LAUNCH(ctx);
+        float *whi = (float *)wt, *wlo = whi + (size_t)M * ldk;
+        k_split_pad_rows<<<grid_for(ctx, (int64_t)M * ldk), 256, 0, ctx->stream>>>(w, whi, wlo, M, K, ldk);
+        LONNX_CHECK_LAUNCH(ctx);
+        rc = P < (1ll << 31) ? gemm_tc(ctx, (const float *)col, whi, wlo, bias, (float *)tmp, (int)P, M, ldk, ldk, ldk,
+                                       M, 1.0f, 1.0f, relu ? LONNX_EPI_RELU : LONNX_EPI_NONE)
+                             : LONNX_E_UNSUPPORTED;
+        if (rc == LONNX_OK) {
+            const int64_t shp[3] = {N, (int64_t)Ho * Wo, M}, perm[3] = {0, 2, 1};
+            rc = transpose_launch(ctx, tmp, 4, shp, 3, perm, y);
+        }
+        ctx_free(ctx, col);
+        ctx_free(ctx, wt);
+        ctx_free(ctx, tmp);
+        if (rc != LONNX_E_UNSUPPORTED) return rc;
+    }
     k_conv2d_direct<<<grid_for(ctx, total), 256, 0, ctx->stream>>>(x, w, bias, y, N, C, H, W, M, kh, kw, sh, sw, pt,
                                                                      pl, dh, dw, group, Ho, Wo, relu);
     LONNX_CHECK_LAUNCH(ctx);

@@ -120,7 +120,7 @@ struct NodeDef {
     }
 };
 
-enum StepKind { S_NODE, S_GEMM, S_LN, S_ATTN };
+enum StepKind { S_NODE, S_GEMM, S_LN, S_ATTN, S_CONV_RELU };
 
 struct Step {
     StepKind kind = S_NODE;
@@ -361,7 +361,7 @@ void exec_matmul(lonnx_graph *g, const NodeDef &n) {
     g->env[n.out.at(0)] = y;
 }
 
-void exec_conv(lonnx_graph *g, const NodeDef &n) {
+void exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string *out_name = nullptr) {
     Value x = lookup(g, n.in.at(0)), w = lookup(g, n.in.at(1));
     Value bias;
     const bool has_bias = n.in.size() > 2 && !n.in[2].empty();
@@ -406,8 +406,8 @@ void exec_conv(lonnx_graph *g, const NodeDef &n) {
     Value y = new_dev(g, DT_FLOAT, {N, M, Ho, Wo});
     ck(lonnx_conv2d_f32(g->ctx, (const float *)x.dptr(), (const float *)w.dptr(), has_bias ? (const float *)bias.dptr() : nullptr,
                         (float *)y.dptr_mut(), N, C, H, W, M, kh, kw, (int)strides[0], (int)strides[1], pt, pl, pb, pr,
-                        (int)dil[0], (int)dil[1], group, 0));
-    g->env[n.out.at(0)] = y;
+                        (int)dil[0], (int)dil[1], group, relu));
+    g->env[out_name ? *out_name : n.out.at(0)] = y;
 }
 
 void exec_maxpool(lonnx_graph *g, const NodeDef &n) {
@@ -1134,6 +1134,19 @@ bool match_attn(Matcher &m, int i, Step &st, std::vector<int> &heads_nodes) {
     return true;
 }
 
+// Conv -> Relu (Conv output used only by the Relu)
+bool match_conv_relu(Matcher &m, int i, Step &st) {
+    const NodeDef &c = m.N(i);
+    if (c.op != "Conv") return false;
+    int r = m.only_consumer(c.out[0]);
+    if (!m.free(r) || m.N(r).op != "Relu") return false;
+    st = Step();
+    st.kind = S_CONV_RELU;
+    st.nodes = {i, r};
+    st.y = m.N(r).out[0];
+    return true;
+}
+
 void build_steps(lonnx_graph *g, bool fuse) {
     g->steps.clear();
     const int n = (int)g->nodes.size();
@@ -1171,6 +1184,11 @@ void build_steps(lonnx_graph *g, bool fuse) {
         if (m.used[i]) continue;
         Step st;
         if (match_ln(m, i, st)) { claim(st); continue; }
+    }
+    for (int i = 0; i < n; ++i) {
+        if (m.used[i]) continue;
+        Step st;
+        if (match_conv_relu(m, i, st)) { claim(st); continue; }
     }
     // weight re-layout for GEMM groups: W [K, N] -> [N, K]
     for (auto &st : groups) {
@@ -1252,6 +1270,7 @@ void run_steps(lonnx_graph *g) {
         case S_GEMM: done = exec_gemm_step(g, s); break;
         case S_LN: done = exec_ln_step(g, s); break;
         case S_ATTN: done = exec_attn_step(g, s); break;
+        case S_CONV_RELU: exec_conv(g, g->nodes[s.nodes[0]], 1, &s.y); done = true; break;
         default: break;
         }
         if (!done) {

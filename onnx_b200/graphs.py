@@ -220,3 +220,79 @@ def e5_flops_per_seq(layers=12, hidden=384, ffn=1536, seq=128):
     products (2 FLOP per multiply-add)."""
     return layers * (2 * seq * hidden * 4 * hidden + 2 * 2 * seq * hidden * ffn
                      + 2 * 2 * seq * seq * hidden)
+
+
+def resnet50(num_classes=1000, seed=0) -> GraphDef:
+    """ResNet-50 v1: stride on the first 1x1 of each
+    downsampling bottleneck, BatchNorm folded into each conv's weight scale and
+    bias (Kaiming-normal weights; the folded BN scale is 0.2 on the last conv
+    of each residual branch and 0.5 on projection shortcuts, which keeps
+    activations O(1) through the 16 residual sums as trained BNs do), global average pool as ReduceMean over H and W,
+    final 2048 x num_classes MatMul + bias.  Convs carry explicit
+    strides/pads; run them with the attributes applied
+    (ComputationalGraph(..., honor_conv_attrs=True)), which the reference's
+    Conv dispatch does not do (Node.cs:137-138)."""
+    rng = np.random.default_rng(seed)
+    inits, nodes = {}, []
+    cnt = [0]
+
+    def conv(x, cin, cout, k, s, pad, relu, gamma=1.0):
+        i = cnt[0]
+        cnt[0] += 1
+        w, b = f"conv{i}.w", f"conv{i}.b"
+        std = gamma * np.sqrt(2.0 / (cin * k * k))
+        inits[w] = (rng.standard_normal((cout, cin, k, k), dtype=np.float32) * std).astype(np.float32)
+        inits[b] = (rng.standard_normal(cout, dtype=np.float32) * 0.01).astype(np.float32)
+        y = f"conv{i}.y"
+        nodes.append(Node("Conv", [x, w, b], [y], {"kernel_shape": [k, k], "strides": [s, s],
+                                                    "pads": [pad] * 4, "auto_pad": "NOTSET", "group": 1,
+                                                    "dilations": [1, 1]}))
+        if relu:
+            nodes.append(Node("Relu", [y], [y + ".relu"]))
+            return y + ".relu"
+        return y
+
+    x = conv("data", 3, 64, 7, 2, 3, True)
+    nodes.append(Node("MaxPool", [x], ["pool0"], {"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1],
+                                                  "auto_pad": "NOTSET"}))
+    x, cin = "pool0", 64
+    for stage, (blocks, width) in enumerate([(3, 64), (4, 128), (6, 256), (3, 512)]):
+        for blk in range(blocks):
+            s = 2 if (blk == 0 and stage > 0) else 1
+            cout = width * 4
+            h = conv(x, cin, width, 1, s, 0, True)
+            h = conv(h, width, width, 3, 1, 1, True)
+            h = conv(h, width, cout, 1, 1, 0, False, gamma=0.2)
+            sc = conv(x, cin, cout, 1, s, 0, False, gamma=0.5) if (blk == 0) else x
+            name = f"res{stage}_{blk}"
+            nodes.append(Node("Add", [h, sc], [name + ".sum"]))
+            nodes.append(Node("Relu", [name + ".sum"], [name]))
+            x, cin = name, cout
+    inits["gap_axes"] = np.array([2, 3], np.int64)
+    nodes.append(Node("ReduceMean", [x, "gap_axes"], ["gap"], {"keepdims": 0}))
+    inits["fc.w"] = (rng.standard_normal((2048, num_classes), dtype=np.float32) * np.sqrt(1.0 / 2048)).astype(np.float32)
+    inits["fc.b"] = np.zeros(num_classes, np.float32)
+    nodes.append(Node("MatMul", ["gap", "fc.w"], ["fc.mm"]))
+    nodes.append(Node("Add", ["fc.mm", "fc.b"], ["logits"]))
+    return GraphDef(nodes, inits, ["data"], ["logits"], opset=18)
+
+
+def resnet50_flops_per_img(h=224, w=224):
+    """Conv + FC FLOPs of resnet50() per image (2 per multiply-add)."""
+    g = resnet50()
+    shapes = {"data": (3, h, w)}
+    total = 0
+    for n in g.nodes:
+        if n.op == "Conv":
+            c, hh, ww = shapes[n.inputs[0]]
+            wt = g.initializers[n.inputs[1]]
+            k, s, p = n.attrs["kernel_shape"][0], n.attrs["strides"][0], n.attrs["pads"][0]
+            ho, wo = (hh + 2 * p - k) // s + 1, (ww + 2 * p - k) // s + 1
+            total += 2 * ho * wo * wt.shape[0] * c * k * k
+            shapes[n.outputs[0]] = (wt.shape[0], ho, wo)
+        elif n.op == "MaxPool":
+            c, hh, ww = shapes[n.inputs[0]]
+            shapes[n.outputs[0]] = (c, (hh + 2 - 3) // 2 + 1, (ww + 2 - 3) // 2 + 1)
+        elif n.op in ("Relu", "Add") and n.inputs[0] in shapes:
+            shapes[n.outputs[0]] = shapes[n.inputs[0]]
+    return total + 2 * 2048 * 1000

@@ -78,3 +78,19 @@ def test_mnist8_synthetic_vs_oracle(ctx):
     x = np.random.default_rng(4).uniform(0, 1, (1, 1, 28, 28)).astype(np.float32)
     got = ComputationalGraph(g, ctx).execute({"Input3": x})["Plus214_Output_0"]
     assert np.array_equal(got, O.execute(g, {"Input3": x})["Plus214_Output_0"])
+
+
+def test_resnet50_vs_oracle(ctx):
+    """ResNet-50 v1 at a small input: strided/padded
+    tensor-core convs with fused bias+ReLU, MaxPool, residual Adds, global
+    average pool, FC -- against the oracle with Conv attributes applied (the
+    reference drops them, so this parity is against the ONNX semantics the
+    oracle restates)."""
+    from onnx_b200 import graphs as G
+    from onnx_b200.graph import ComputationalGraph
+    g = G.resnet50(seed=1)
+    x = np.random.default_rng(1).uniform(0, 1, (2, 3, 96, 96)).astype(np.float32)
+    cg = ComputationalGraph(g, ctx, honor_conv_attrs=True)
+    got = cg.execute({"data": x})["logits"]
+    ref = O.execute(g, {"data": x}, honor_conv_attrs=True)["logits"]
+    close(got, ref)

@@ -269,3 +269,27 @@ def test_attention_direct(ctx):
                                       B, S, h, dh, np.float32(np.sqrt(dh))))
     ctx.sync()
     close(out.to_host(), ref, atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("xs,ws,stride,pad,relu", [((4, 64, 28, 28), (128, 64, 3, 3), 1, 1, 1),
+                                                   ((2, 3, 64, 64), (64, 3, 7, 7), 2, 3, 1),
+                                                   ((4, 256, 14, 14), (512, 256, 1, 1), 2, 0, 0),
+                                                   ((3, 32, 17, 19), (48, 32, 3, 3), 1, 1, 0)])
+def test_conv_tensor_core_path_vs_oracle(ctx, xs, ws, stride, pad, relu):
+    """Convs large enough for the tensor-core GEMM formulation (im2col rows,
+    3xTF32, per-channel bias + ReLU epilogue, NHWC -> NCHW)."""
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    rng = np.random.default_rng(xs[1] + ws[0])
+    x = rng.uniform(-1, 1, xs).astype(np.float32)
+    w = (rng.standard_normal(ws) * np.sqrt(2.0 / np.prod(ws[1:]))).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, ws[0]).astype(np.float32)
+    ref = O.conv(x, w, b, auto_pad="NOTSET", pads=[pad] * 4, strides=[stride] * 2)
+    if relu:
+        ref = O.unary("Relu", ref)
+    dx, dw, db = (DeviceTensor.from_host(ctx, a) for a in (x, w, b))
+    y = DeviceTensor(ctx, ref.shape, np.float32)
+    N.check(N.lib.lonnx_conv2d_f32(ctx.handle, dx.ptr, dw.ptr, db.ptr, y.ptr, xs[0], xs[1], xs[2], xs[3], ws[0],
+                                   ws[2], ws[3], stride, stride, pad, pad, pad, pad, 1, 1, 1, relu))
+    ctx.sync()
+    close(y.to_host(), ref)
