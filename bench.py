@@ -209,8 +209,44 @@ def mnist_latency(ctx, st, torch, reps=200):
     e1.record(st)
     e1.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / reps
+    cg.capture()
+    for _ in range(10):
+        cg.replay()
+    e0.record(st)
+    for _ in range(reps):
+        cg.replay()
+    e1.record(st)
+    e1.synchronize()
+    us_g = e0.elapsed_time(e1) * 1e3 / reps
     return {"metric": "MNIST-8 CNN img/s at batch 1 (device-resident input)", "img_per_s": round(1e6 / us, 1),
-            "us_per_img": round(us, 2), "flops_per_img": 1573120}
+            "us_per_img": round(us, 2), "img_per_s_cuda_graph": round(1e6 / us_g, 1),
+            "us_per_img_cuda_graph": round(us_g, 2), "flops_per_img": 1573120}
+
+
+def resnet_throughput(ctx, st, torch, batch=64, reps=5):
+    """ResNet-50 v1 at batch 64 x 3 x 224 x 224,
+    device-resident input, img/s over `reps` forwards."""
+    from onnx_b200 import graphs as G
+    from onnx_b200.graph import ComputationalGraph
+    from onnx_b200.tensor import DeviceTensor
+    g = G.resnet50(seed=0)
+    cg = ComputationalGraph(g, ctx, honor_conv_attrs=True)
+    x = DeviceTensor.from_host(ctx, np.random.default_rng(0).uniform(0, 1, (batch, 3, 224, 224)).astype(np.float32))
+    cg.set_inputs({"data": x})
+    for _ in range(2):
+        cg.run()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        cg.run()
+    e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    fl = G.resnet50_flops_per_img()
+    return {"metric": "ResNet-50 v1 img/s at batch 64 x 224^2 (device-resident input)",
+            "img_per_s": round(batch / (ms * 1e-3), 1), "ms_per_batch": round(ms, 2),
+            "tflops_algorithmic": round(fl * batch / (ms * 1e-3) / 1e12, 2)}
 
 
 def main():
@@ -222,6 +258,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--vocab", type=int, default=250037)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-resnet", action="store_true")
     ap.add_argument("--profile-case", type=int, default=0, metavar="B",
                     help="run two 2-layer e5 forwards at batch B and exit (small case for ncu captures)")
     args = ap.parse_args()
@@ -296,6 +333,7 @@ def main():
 
     roof = gemm_roofline(ctx, st, torch) if rank == 0 else None
     mnist = mnist_latency(ctx, st, torch) if rank == 0 else None
+    resnet = resnet_throughput(ctx, st, torch) if rank == 0 and not args.no_resnet else None
     clocks = clk.summary()
     if rank == 0:
         cb = None if args.no_cpu_baseline else cpu_baseline(8)
@@ -313,7 +351,7 @@ def main():
                 "e2e": {"value": round(world * B / (e2e_ms * 1e-3), 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches * world, "gpu_launches_per_step_per_gpu": launches // args.steps, "roofline": roof, "cpu_baseline": cb, "clocks": clocks,
-                "flops_per_seq": G.e5_flops_per_seq(), "mnist": mnist}
+                "flops_per_seq": G.e5_flops_per_seq(), "mnist": mnist, "resnet50": resnet}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -209,6 +209,13 @@ LONNX_API int lonnx_graph_output_device(lonnx_graph *g, const char *name, const 
 LONNX_API int lonnx_graph_get_output(lonnx_graph *g, const char *name, void *host, size_t bytes);
 /* Release intermediates back to the allocator (ComputationalGraph.Reset, :336-349). */
 LONNX_API int lonnx_graph_reset(lonnx_graph *g);
+/* Record one execution (inputs already set, shapes then fixed) as a CUDA
+ * graph; lonnx_graph_replay re-runs it with one launch.  Buffers used by the
+ * captured execution stay reserved for the graph until the next capture,
+ * lonnx_graph_reset or lonnx_graph_destroy; device inputs must stay at the
+ * same addresses (update their contents in place between replays). */
+LONNX_API int lonnx_graph_capture(lonnx_graph *g);
+LONNX_API int lonnx_graph_replay(lonnx_graph *g);
 /* Nodes after fusion (kernels launched per execute, for reporting). */
 LONNX_API int lonnx_graph_num_steps(lonnx_graph *g);
 

@@ -72,6 +72,8 @@ _SIGS = {
     "lonnx_graph_output_device": (c_int, [c_vp, c_char_p, ctypes.POINTER(c_vp)]),
     "lonnx_graph_get_output": (c_int, [c_vp, c_char_p, c_vp, c_size]),
     "lonnx_graph_reset": (c_int, [c_vp]),
+    "lonnx_graph_capture": (c_int, [c_vp]),
+    "lonnx_graph_replay": (c_int, [c_vp]),
     "lonnx_graph_num_steps": (c_int, [c_vp]),
 }
 

@@ -155,6 +155,10 @@ struct lonnx_graph {
     std::map<std::string, Value> env;
     std::vector<Step> steps;
     bool prepared = false;
+    // CUDA-graph capture of one execution (lonnx_graph_capture / _replay)
+    cudaGraphExec_t exec = nullptr;
+    std::vector<void *> held;                    // blocks the captured graph uses
+    std::map<std::string, Value> captured_outputs;
     bool honor_conv_attrs = false;
     int opset = 13;
 };
@@ -1310,9 +1314,82 @@ Value make_value(lonnx_graph *g, int dtype, const int64_t *shape, int rank, cons
     return v;
 }
 
+void release_capture(lonnx_graph *g) {
+    if (g->exec) {
+        cudaStreamSynchronize(g->ctx->stream);
+        cudaGraphExecDestroy(g->exec);
+        g->exec = nullptr;
+    }
+    g->captured_outputs.clear();
+    for (void *p : g->held) ctx_free(g->ctx, p);
+    g->held.clear();
+}
+
 }  // namespace
 
 extern "C" {
+
+LONNX_API int lonnx_graph_capture(lonnx_graph *g) {
+    if (!g) return set_error(LONNX_E_BADARG, "null graph");
+    int rc = device_guard(g->ctx);
+    if (rc) return rc;
+    return guarded([&]() -> int {
+        if (!g->prepared) build_steps(g, false), g->prepared = true;
+        release_capture(g);
+        lonnx_ctx *c = g->ctx;
+        g->env.clear();
+        LONNX_CUDA(cudaStreamSynchronize(c->stream));
+        LONNX_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+        c->capturing = true;
+        int err = LONNX_OK;
+        std::string msg;
+        try {
+            run_steps(g);
+            for (auto &o : g->outputs)
+                if (!has_value(g, o)) fail(LONNX_E_BADARG, "graph output " + o + " was not produced");
+        } catch (const OpError &e) {
+            err = e.code;
+            msg = e.what();
+        }
+        cudaGraph_t graph = nullptr;
+        cudaError_t ce = cudaStreamEndCapture(c->stream, &graph);
+        c->capturing = false;
+        g->held.swap(c->capture_hold);
+        c->capture_hold.clear();
+        if (err) {
+            if (graph) cudaGraphDestroy(graph);
+            g->env.clear();
+            release_capture(g);
+            fail(err, "capture failed: " + msg);
+        }
+        if (ce != cudaSuccess) {
+            cudaGetLastError();
+            release_capture(g);
+            fail(LONNX_E_CUDA, std::string("capture failed: ") + cudaGetErrorString(ce));
+        }
+        ce = cudaGraphInstantiate(&g->exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ce != cudaSuccess) {
+            cudaGetLastError();
+            release_capture(g);
+            fail(LONNX_E_CUDA, std::string("graph instantiate failed: ") + cudaGetErrorString(ce));
+        }
+        for (auto &o : g->outputs) g->captured_outputs[o] = lookup(g, o);
+        g->env = g->captured_outputs;
+        return LONNX_OK;
+    });
+}
+
+LONNX_API int lonnx_graph_replay(lonnx_graph *g) {
+    if (!g) return set_error(LONNX_E_BADARG, "null graph");
+    if (!g->exec) return set_error(LONNX_E_BADARG, "graph was not captured");
+    int rc = device_guard(g->ctx);
+    if (rc) return rc;
+    LONNX_CUDA(cudaGraphLaunch(g->exec, g->ctx->stream));
+    g->ctx->launches++;
+    g->env = g->captured_outputs;
+    return LONNX_OK;
+}
 
 LONNX_API int lonnx_graph_create(lonnx_ctx *ctx, lonnx_graph **out) {
     int rc = device_guard(ctx);
@@ -1328,6 +1405,7 @@ LONNX_API int lonnx_graph_destroy(lonnx_graph *g) {
     if (!g) return LONNX_OK;
     device_guard(g->ctx);
     cudaStreamSynchronize(g->ctx->stream);
+    release_capture(g);
     delete g;
     return LONNX_OK;
 }
@@ -1501,6 +1579,7 @@ LONNX_API int lonnx_graph_get_output(lonnx_graph *g, const char *name, void *hos
 
 LONNX_API int lonnx_graph_reset(lonnx_graph *g) {
     if (!g) return set_error(LONNX_E_BADARG, "null graph");
+    release_capture(g);
     g->env.clear();
     g->inputs.clear();
     return LONNX_OK;

@@ -8,6 +8,7 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 #include "../../include/lonnx.h"
 
@@ -41,6 +42,10 @@ struct lonnx_ctx {
     size_t scratch_bytes = 0;
     void *scratch2 = nullptr;
     size_t scratch2_bytes = 0;
+    // while a graph is being captured, freed blocks are held (their addresses
+    // are baked into the captured graph) instead of returning to the cache
+    bool capturing = false;
+    std::vector<void *> capture_hold;
 };
 
 namespace lonnx {

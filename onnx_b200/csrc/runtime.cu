@@ -81,6 +81,10 @@ int ctx_free(lonnx_ctx *ctx, void *p) {
     Allocator &A = ctx->alloc;
     auto it = A.live.find(p);
     if (it == A.live.end()) return set_error(LONNX_E_BADARG, "lonnx_free: pointer %p not allocated by this context", p);
+    if (ctx->capturing) {
+        ctx->capture_hold.push_back(p);  // stays live until the captured graph is released
+        return LONNX_OK;
+    }
     A.free_blocks.emplace(it->second, p);
     A.live.erase(it);
     return LONNX_OK;

@@ -86,6 +86,14 @@ class ComputationalGraph:
         """Enqueue one execution of the whole graph (no host synchronisation)."""
         N.check(N.lib.lonnx_graph_execute(self.handle))
 
+    def capture(self):
+        """Record one execution as a CUDA graph (inputs must already be set)."""
+        N.check(N.lib.lonnx_graph_capture(self.handle))
+
+    def replay(self):
+        """Re-run the captured execution with a single graph launch."""
+        N.check(N.lib.lonnx_graph_replay(self.handle))
+
     def output_shape(self, name):
         shp = (ctypes.c_int64 * 8)()
         r = ctypes.c_int()

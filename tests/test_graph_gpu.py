@@ -94,3 +94,26 @@ def test_resnet50_vs_oracle(ctx):
     got = cg.execute({"data": x})["logits"]
     ref = O.execute(g, {"data": x}, honor_conv_attrs=True)["logits"]
     close(got, ref)
+
+
+@pytest.mark.parametrize("which", ["mnist8", "e5"])
+def test_cuda_graph_replay_matches_execute(ctx, which):
+    from onnx_b200 import graphs as G
+    from onnx_b200.graph import ComputationalGraph
+    from onnx_b200.tensor import DeviceTensor
+    if which == "mnist8":
+        g = G.mnist8(seed=5)
+        host = {"Input3": np.random.default_rng(5).uniform(0, 1, (1, 1, 28, 28)).astype(np.float32)}
+    else:
+        g = G.e5_encoder(layers=2, vocab=3000, seq=64, seed=5)
+        host = G.e5_inputs(4, 64, 3000, seed=5)
+    cg = ComputationalGraph(g, ctx)
+    ref = cg.execute(host)
+    dev = {k: DeviceTensor.from_host(ctx, v) for k, v in host.items()}
+    cg.set_inputs(dev)
+    cg.run()
+    cg.capture()
+    for _ in range(3):
+        cg.replay()
+    for o in g.outputs:
+        assert np.array_equal(cg.output(o), ref[o])
