@@ -432,14 +432,14 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
     if (rc) return rc;
     rc = make_map(&mwlo, Wlo, N, K, ldw, bn);
     if (rc) return rc;
-    // A's low parts: split inside the kernel per tile (default), or streamed
-    // once into scratch and TMA-loaded beside A when many N tiles would each
-    // repeat the split (N >= 3072).  LONNX_GEMM_ALO=0/1 forces either.
+    // A's low parts: split inside the kernel per tile (default; measured
+    // faster on every BASELINE shape), or streamed once into scratch and
+    // TMA-loaded beside A (LONNX_GEMM_ALO=1).
     static const int mode = [] {
         const char *e = getenv("LONNX_GEMM_ALO");
         return e ? atoi(e) : -1;
     }();
-    const bool alo = mode < 0 ? N >= 3072 : mode != 0;
+    const bool alo = mode > 0;
     if (alo && allow_scratch) {
         // A_lo streamed into scratch, then TMA-loaded beside A
         void *tmp = nullptr;
