@@ -194,6 +194,11 @@ template <int DH>
 int launch_attn(lonnx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld,
                 const float *mask, float *out, int B, int S, int heads, float scale) {
     static const bool exact = getenv("LONNX_ATTN_EXACT") != nullptr;
+    static const bool simt = getenv("LONNX_ATTN_SIMT") != nullptr || getenv("LONNX_DISABLE_TC") != nullptr;
+    if (!exact && !simt) {
+        const int rc = lonnx::attention_tc(ctx, q, k, v, ld, mask, out, B, S, heads, DH, scale);
+        if (rc != LONNX_E_UNSUPPORTED) return rc;
+    }
     dim3 grid((S + QT - 1) / QT, B * heads);
     if (!exact) {
         const size_t smem = ((size_t)2 * S * DH + S) * sizeof(float);

@@ -1,0 +1,248 @@
+// Fused attention of one BERT layer on sm_100a tensor cores (S <= 128, dh = 32).
+//
+// One CTA (4 warps) per (batch, head):
+//   1. each thread loads one row of Q, K and V (16-byte vector loads from the
+//      [B, S, ld] projection output, head h at column h*dh) and writes
+//      Q, Q_lo, K, K_lo (K-major, 128-byte swizzle) and V^T, V^T_lo (the B
+//      operand of P.V, keys along K) into shared memory, where x_lo =
+//      x - tf32(x) (3xTF32 split; the raw value serves as the tf32 high part);
+//   2. one thread issues S = Q K^T as 4 K-steps x {Q_lo.K, Q.K_lo, Q.K}
+//      (tcgen05.mma kind::tf32, 128 x 128 x 8) into TMEM columns [0, 128);
+//   3. each thread owns one query row = one TMEM lane: pass 1 reads its 128
+//      scores (tcgen05.ld) for the row max (starting at 0, as the reference's
+//      ReduceMax); then for each half of 64 keys it forms
+//      e = exp(s/scale + mask - max), sums them and writes E, E_lo into
+//      shared memory (over the Q/K buffers, free by then), and
+//   4. one thread issues O += E V for that half as 8 K-steps x 3 products
+//      (128 x 32 x 8) into TMEM columns [128, 160);
+//   5. each thread reads its O row, divides by its row sum, stores 128 bytes.
+// ~98 KB of shared memory, so two CTAs share an SM.
+// The [B, heads, S, S] score tensor never leaves the SM.  Replaces the
+// MatMul -> Div -> Add -> Softmax -> MatMul node chain and the Transpose /
+// Reshape nodes around it (src/Lokad.Onnx.Tensors/TensorOps.cs:600-704,
+// 1312-1330, 1358-1407).  Every wait is bounded; on expiry the CTA records
+// LONNX_E_TIMEOUT, drains its MMAs, frees TMEM and returns.
+#include "lonnx_internal.cuh"
+#include "tc_common.cuh"
+
+namespace {
+
+using namespace lonnx::tc;
+
+constexpr int AT = 128;          // threads = query rows per CTA
+constexpr int DH = 32;
+constexpr int ROWB = 128;        // bytes per swizzled row (32 fp32)
+constexpr int TILE = 128 * ROWB; // 16 KB: 128 rows x 32 fp32
+// shared memory map (bytes)
+constexpr int OFF_Q = 0, OFF_QLO = TILE, OFF_K = 2 * TILE, OFF_KLO = 3 * TILE;
+constexpr int OFF_E = 0;              // E of 64 keys: 2 K-atoms x 16 KB (over Q/K after S is done)
+constexpr int OFF_ELO = 2 * TILE;     // E_lo: 2 x 16 KB
+constexpr int OFF_VT = 4 * TILE;      // V^T: 4 K-atoms x [32 rows x 128 B]
+constexpr int OFF_VTLO = OFF_VT + 4 * 32 * ROWB;
+constexpr int OFF_MASK = OFF_VTLO + 4 * 32 * ROWB;
+constexpr int OFF_BAR = OFF_MASK + 128 * 4;
+constexpr int SMEM = OFF_BAR + 64 + 1024;
+
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+__device__ __forceinline__ float4 lo4(float4 v) {
+    return make_float4(__fsub_rn(v.x, tf32_hi(v.x)), __fsub_rn(v.y, tf32_hi(v.y)), __fsub_rn(v.z, tf32_hi(v.z)),
+                       __fsub_rn(v.w, tf32_hi(v.w)));
+}
+// byte offset of 16-byte chunk c of row r in a 128B-swizzled K-major tile
+__device__ __forceinline__ int swz(int r, int c) { return r * ROWB + ((c ^ (r & 7)) << 4); }
+
+__global__ void __launch_bounds__(AT, 2)
+k_attention_tc(const float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v, int64_t ld,
+               const float *__restrict__ maskadd, float *__restrict__ out, int S, int heads, float scale,
+               int *dev_flags) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3);
+    float *msk = reinterpret_cast<float *>(sm + OFF_MASK);
+    const int t = threadIdx.x, warp = t >> 5;
+    const int bh = blockIdx.x;
+    const int b = bh / heads, h = bh % heads;
+    const int64_t base = (int64_t)b * S * ld + (int64_t)h * DH;
+    const uint32_t bar_s = smem_u32(bars), bar_o = smem_u32(bars + 1), bar_drain = smem_u32(bars + 2);
+
+    if (t == 0) {
+        mbar_init(bar_s, 1);
+        mbar_init(bar_o, 1);
+        mbar_init(bar_drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), 256);
+        tmem_relinquish();
+    }
+    // ---- 1. operands into shared memory --------------------------------------
+    {
+        const bool live = t < S;
+        const float *qr = q + base + (int64_t)t * ld, *kr = k + base + (int64_t)t * ld, *vr = v + base + (int64_t)t * ld;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 qv = live ? __ldg(reinterpret_cast<const float4 *>(qr) + c) : z;
+            const float4 kv = live ? __ldg(reinterpret_cast<const float4 *>(kr) + c) : z;
+            *reinterpret_cast<float4 *>(sm + OFF_Q + swz(t, c)) = qv;
+            *reinterpret_cast<float4 *>(sm + OFF_QLO + swz(t, c)) = lo4(qv);
+            *reinterpret_cast<float4 *>(sm + OFF_K + swz(t, c)) = kv;
+            *reinterpret_cast<float4 *>(sm + OFF_KLO + swz(t, c)) = lo4(kv);
+        }
+        // V^T: key t is column t of the [32 x 128] B operand: K-atom t/32,
+        // row d, 16-byte chunk (t%32)/4, word t%4
+        const int atom = t >> 5, ch = (t & 31) >> 2, wd = t & 3;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const float4 vv = live ? __ldg(reinterpret_cast<const float4 *>(vr) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float e4[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int d = c * 4 + u;
+                const int off = atom * 32 * ROWB + swz(d, ch) + wd * 4;
+                *reinterpret_cast<float *>(sm + OFF_VT + off) = e4[u];
+                *reinterpret_cast<float *>(sm + OFF_VTLO + off) = __fsub_rn(e4[u], tf32_hi(e4[u]));
+            }
+        }
+        msk[t] = (maskadd && live) ? maskadd[(int64_t)b * S + t] : 0.0f;
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    bool ok = true;
+
+    // ---- 2. S = Q K^T ------------------------------------------------------------
+    if (t == 0) {
+        constexpr uint32_t idesc = idesc_tf32(128, 128);
+        const uint32_t a = smem_u32(sm + OFF_Q), al = smem_u32(sm + OFF_QLO);
+        const uint32_t bk = smem_u32(sm + OFF_K), bl = smem_u32(sm + OFF_KLO);
+#pragma unroll
+        for (int kk = 0; kk < DH / 8; ++kk) {
+            const uint32_t ko = kk * 32;
+            mma_tf32(tmem, smem_desc_sw128(al + ko), smem_desc_sw128(bk + ko), idesc, kk != 0);
+            mma_tf32(tmem, smem_desc_sw128(a + ko), smem_desc_sw128(bl + ko), idesc, 1);
+            mma_tf32(tmem, smem_desc_sw128(a + ko), smem_desc_sw128(bk + ko), idesc, 1);
+        }
+        mma_commit(bar_s);
+    }
+    if (!mbar_wait(bar_s, 0, nullptr)) ok = false;
+    tc_fence_after();
+
+    // ---- 3. softmax rows straight from TMEM ----------------------------------
+    const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+    const float inv_scale = 1.0f / scale;
+    float mx = 0.0f;
+    if (ok) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(lane_addr + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int key = c * 32 + j;
+                if (key < S) mx = fmaxf(mx, __uint_as_float(r[j]) * inv_scale + msk[key]);
+            }
+        }
+    }
+    // ---- 3b/4. two halves of 64 keys: e -> E (shared memory) -> O += E V ----
+    float sum = 0.0f;
+    for (int hf = 0; hf < 2; ++hf) {
+        if (ok) {
+#pragma unroll
+            for (int c2 = 0; c2 < 2; ++c2) {
+                const int c = hf * 2 + c2;
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(lane_addr + c * 32, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) {
+                    float e[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int key = c * 32 + ch * 4 + u;
+                        e[u] = key < S ? expf(__uint_as_float(r[ch * 4 + u]) * inv_scale + msk[key] - mx) : 0.0f;
+                        sum += e[u];
+                    }
+                    const float4 ev = make_float4(e[0], e[1], e[2], e[3]);
+                    // E is the A operand of E.V: row t, K-atom c2, chunk ch
+                    *reinterpret_cast<float4 *>(sm + OFF_E + c2 * TILE + swz(t, ch)) = ev;
+                    *reinterpret_cast<float4 *>(sm + OFF_ELO + c2 * TILE + swz(t, ch)) = lo4(ev);
+                }
+            }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (t == 0 && ok) {
+            constexpr uint32_t idesc = idesc_tf32(128, DH);
+            const uint32_t oacc = tmem + 128;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t atom = kk >> 2, ko = (kk & 3) * 32, vatom = hf * 2 + atom;
+                const uint32_t a = smem_u32(sm + OFF_E + atom * TILE) + ko, al = smem_u32(sm + OFF_ELO + atom * TILE) + ko;
+                const uint32_t bv = smem_u32(sm + OFF_VT + vatom * 32 * ROWB) + ko;
+                const uint32_t bl = smem_u32(sm + OFF_VTLO + vatom * 32 * ROWB) + ko;
+                mma_tf32(oacc, smem_desc_sw128(al), smem_desc_sw128(bv), idesc, (hf | kk) != 0);
+                mma_tf32(oacc, smem_desc_sw128(a), smem_desc_sw128(bl), idesc, 1);
+                mma_tf32(oacc, smem_desc_sw128(a), smem_desc_sw128(bv), idesc, 1);
+            }
+            mma_commit(bar_o);
+        }
+        // E is overwritten by the next half only after these MMAs are done
+        if (ok && !mbar_wait(bar_o, hf & 1, nullptr)) ok = false;
+        tc_fence_after();
+    }
+
+    // ---- 5. O row / sum -> out[b, t, h*32 ..] ------------------------------------
+    if (ok) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(lane_addr + 128, r);
+        tmem_ld_wait();
+        if (t < S) {
+            const float inv = 1.0f / sum;
+            float *op = out + ((int64_t)b * S + t) * ((int64_t)heads * DH) + (int64_t)h * DH;
+#pragma unroll
+            for (int d = 0; d < DH; d += 4)
+                *reinterpret_cast<float4 *>(op + d) =
+                    make_float4(__uint_as_float(r[d]) * inv, __uint_as_float(r[d + 1]) * inv,
+                                __uint_as_float(r[d + 2]) * inv, __uint_as_float(r[d + 3]) * inv);
+        }
+    } else {
+        if (t == 0) atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
+        if (t == 0) {
+            mma_commit(bar_drain);
+            mbar_wait(bar_drain, 0, nullptr, 400000000ll);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
+}  // namespace
+
+namespace lonnx {
+
+// Returns LONNX_E_UNSUPPORTED when the shape does not fit this kernel.
+int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld, const float *mask,
+                 float *out, int B, int S, int heads, int dh, float scale) {
+    if (dh != DH || S <= 0 || S > 128) return LONNX_E_UNSUPPORTED;
+    static bool attr_set[64] = {false};
+    if (!attr_set[ctx->device & 63]) {
+        LONNX_CUDA(cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        attr_set[ctx->device & 63] = true;
+    }
+    k_attention_tc<<<B * heads, AT, SMEM, ctx->stream>>>(q, k, v, ld, mask, out, S, heads, scale, ctx->dev_flags);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+}  // namespace lonnx

@@ -87,6 +87,9 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
 // hi = w with the low 13 mantissa bits cleared, lo = w - hi (exact).
 int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans);
 int64_t gemm_tc_min_work();
+// Fused attention on tensor cores (dh = 32, S <= 128); LONNX_E_UNSUPPORTED otherwise.
+int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld, const float *mask,
+                 float *out, int B, int S, int heads, int dh, float scale);
 int gemm_simt(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
               int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
               float alpha, float beta, int epi, const float *residual);
