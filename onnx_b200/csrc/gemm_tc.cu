@@ -9,17 +9,18 @@
 // the tile product accumulates hi.hi + hi.lo + lo.hi -- the published 3xTF32
 // scheme, which keeps fp32-level accuracy (the dropped lo.lo term is ~2^-22
 // relative).  The weight is split once, ahead of time (split_tf32_nk); the
-// activation tile is split in shared memory right after its TMA load, so HBM
-// traffic for A is that of a plain fp32 GEMM.
+// activation tile is split on chip right after its TMA load, so HBM traffic
+// for A is that of a plain fp32 GEMM.
 //
-// CTA = 12 warps, one 128 x BN output tile (BN = 128 or 192):
+// CTA = 20 warps, one 128 x BN output tile (BN = 128 or 192):
 //   warp 0      TMA producer (one lane): A, W_hi, W_lo tiles of 32 K-columns
 //               (128 bytes = one 128B-swizzle row) per stage, 3-4 stages
 //   warp 1      TMEM allocator + MMA issuer (one lane): 4 K-steps x 3
-//               products per stage into one of two TMEM chunk accumulators
-//   warps 2-3   write A_lo of each stage into a 2-buffer ring
-//   warps 4-11  drain each chunk accumulator into fp32 registers (round to
-//               nearest), then run the epilogue: bias, activation, stores
+//               products per stage, A from TMEM, W from shared memory, into
+//               one of two TMEM chunk accumulators
+//   warps 4-7   move each stage's A rows into TMEM as tf32 hi and lo parts
+//   warps 8-19  drain each chunk accumulator into fp32 registers (round to
+//               nearest), 64 columns per warp, then run the epilogue
 // Every mbarrier wait is bounded (~2 s); on expiry the CTA raises an abort
 // flag, records LONNX_E_TIMEOUT in the context's device flags, drains its
 // in-flight copies and MMAs, frees its TMEM, and returns.
@@ -40,66 +41,58 @@ using namespace lonnx::tc;
 constexpr int BM = 128;
 constexpr int BK = 32;                  // fp32 elements per 128-byte row
 constexpr int A_TILE = BM * BK * 4;     // 16 KB
-constexpr int kThreads = 384;           // 12 warps
-// warp roles: 0 TMA, 1 MMA + TMEM owner, 2-3 split A, 4-11 accumulate/epilogue
-constexpr int W_TMA = 0, W_MMA = 1, W_SPLIT0 = 2, N_SPLIT = 2, W_ACC0 = 4, N_ACC = 8;
+constexpr int kThreads = 640;           // 20 warps
+// warp roles: 0 TMA, 1 MMA + TMEM owner, 4-7 A -> TMEM, 8-19 accumulate/epilogue
+constexpr int W_TMA = 0, W_MMA = 1, W_A0 = 4, W_ACC0 = 8;
 
-template <int BN, bool ALO>
+template <int BN>
 struct Cfg {
     static constexpr int W_TILE = BN * BK * 4;
-    // TMA ring: A, W_hi, W_lo (+ A_lo when it comes from HBM)
-    static constexpr int STAGE = (ALO ? 2 : 1) * A_TILE + 2 * W_TILE;
-    static constexpr int LO = ALO ? 0 : 2 * A_TILE;    // in-kernel A_lo ring: 2 buffers
-    static constexpr int STAGES = (4 * STAGE + LO + 1280 <= 227 * 1024) ? 4
-                                  : (3 * STAGE + LO + 1280 <= 227 * 1024) ? 3 : 2;
-    static constexpr int SMEM = STAGES * STAGE + LO + 1024 /*align*/ + 256 /*barriers*/;
-    static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;  // two chunk accumulators
-    static constexpr int COLS_PER_ACC = BN / 2;                  // per accumulator thread
+    static constexpr int STAGE = A_TILE + 2 * W_TILE;  // TMA ring: A, W_hi, W_lo
+    static constexpr int STAGES = (4 * STAGE + 1280 <= 227 * 1024) ? 4 : 3;
+    static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int GROUPS = BN / 64;              // accumulator column groups of 64
+    static constexpr int ACC_COL = 0;                   // TMEM: 2 chunk accumulators [0, 2 BN)
+    static constexpr int A_COL = 2 * BN;                // then NAB A buffers of 64 (hi 32 | lo 32)
+    static constexpr int NAB = 2 * BN + 3 * 64 <= 512 ? 3 : 2;
+    static constexpr int TMEM_COLS = 2 * BN + NAB * 64 <= 256 ? 256 : 512;
 };
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
-// lo_buf <- x - tf32(x).  The tensor core reads an fp32 operand as its tf32
-// truncation (tests/test_gemm_gpu.py::test_tf32_operand_truncation), so the
-// raw tile already serves as the high part.
-__device__ __forceinline__ void split_lo(const uint8_t *buf, uint8_t *lo_buf, int bytes, int tid, int nthreads) {
-#pragma unroll 4
-    for (int off = tid * 16; off < bytes; off += nthreads * 16) {
-        const float4 v = *reinterpret_cast<const float4 *>(buf + off);
-        float4 l;
-        l.x = __fsub_rn(v.x, tf32_hi(v.x));
-        l.y = __fsub_rn(v.y, tf32_hi(v.y));
-        l.z = __fsub_rn(v.z, tf32_hi(v.z));
-        l.w = __fsub_rn(v.w, tf32_hi(v.w));
-        *reinterpret_cast<float4 *>(lo_buf + off) = l;
-    }
-}
-
+// C[M,N] = alpha * A . W^T + beta * bias, epilogue.
+//   A [M,K] fp32 (tmA); W_hi, W_lo [N,K] (tmW, tmWlo): the weight pre-split
+//   into its tf32 part and the exact fp32 remainder.
+// Per 32-wide K stage: 4 K-steps x {A_lo.W_hi, A_hi.W_lo, A_hi.W_hi}, with
+// A_hi and A_lo in TMEM (written by the A warps) and W_hi / W_lo in shared
+// memory (TMA).
+//
+// Why A lives in TMEM: shared-memory bandwidth binds a 3xTF32 tile.  With
+// both operands in shared memory one 32-wide stage moved ~216 KB through it
+// (TMA writes, the split, three MMAs re-reading A and W); with A in TMEM it
+// is ~152 KB, about the MMA time of the stage.
+//
 // Accumulation: each K stage is accumulated by the tensor core into a fresh
 // TMEM buffer (two buffers, ping-pong) and the stage sums are added into fp32
 // registers with round-to-nearest by the accumulator warps.  The tensor
 // core's accumulator rounds toward zero, so one TMEM accumulator over all of
 // K builds an error that grows linearly with K (measured ~10x the
 // sequential fp32 sum at K = 1536); 32-wide chunks keep it at fp32 level.
-//
-// Shared-memory bandwidth is the binding resource of a 3xTF32 tile (operand
-// reads of three MMAs + TMA writes + the split), which is why the weight is
-// split once ahead of time and A_lo has its own 2-buffer ring (so the TMA
-// ring can be 3-4 stages deep).
-template <int BN, bool ALO>
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
-k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAlo,
-              const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmWlo,
-              const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, int ldc, float alpha,
-              float beta, int epi, int *dev_flags) {
-    using G = Cfg<BN, ALO>;
+k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+              const __grid_constant__ CUtensorMap tmWlo, const float *__restrict__ bias, float *__restrict__ C,
+              int M, int N, int K, int ldc, float alpha, float beta, int epi, int *dev_flags) {
+    using G = Cfg<BN>;
     constexpr int S = G::STAGES;
+    constexpr int NACC = 4 * G::GROUPS;  // accumulator warps in use
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * G::STAGE + G::LO);
-    // [0,S) full  [S,2S) split done  [2S,3S) stage free  [3S,3S+2) chunk ready
-    // [3S+2,3S+4) chunk drained  [3S+4] abort drain  [3S+5,3S+7) A_lo buffer free
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 7);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * G::STAGE);
+    // [0,S) full  [S,2S) A in TMEM  [2S,3S) stage free  [3S,3S+2) chunk ready
+    // [3S+2,3S+4) chunk drained  [3S+4] abort drain  [3S+5,3S+5+NAB) TMEM A buffer free
+    constexpr int NAB = G::NAB;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 5 + NAB);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,32 +105,29 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     auto tfull = [&](int b) { return smem_u32(bars + 3 * S + b); };
     auto tdrain = [&](int b) { return smem_u32(bars + 3 * S + 2 + b); };
     const uint32_t drainbar = smem_u32(bars + 3 * S + 4);
-    auto lofree = [&](int b) { return smem_u32(bars + 3 * S + 5 + b); };
+    auto afree = [&](int b) { return smem_u32(bars + 3 * S + 5 + b); };
     auto stageA = [&](int s) { return smem + s * G::STAGE; };
     auto stageW = [&](int s) { return smem + s * G::STAGE + A_TILE; };
     auto stageWlo = [&](int s) { return smem + s * G::STAGE + A_TILE + G::W_TILE; };
-    auto stageAlo = [&](int s) { return smem + s * G::STAGE + A_TILE + 2 * G::W_TILE; };
-    auto bufAlo = [&](int b) { return smem + S * G::STAGE + b * A_TILE; };
     int issued = 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full(s), 1);
-            mbar_init(conv(s), ALO ? 1 : N_SPLIT + N_ACC);
+            mbar_init(conv(s), 4);  // one arrive per A warp
             mbar_init(empty(s), 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull(b), 1);
-            mbar_init(tdrain(b), N_ACC);
-            mbar_init(lofree(b), 1);
+            mbar_init(tdrain(b), NACC);
         }
+        for (int b = 0; b < NAB; ++b) mbar_init(afree(b), 1);
         mbar_init(drainbar, 1);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmW);
         prefetch_tmap(&tmWlo);
-        if (ALO) prefetch_tmap(&tmAlo);
     }
     if (warp == W_MMA) {
         tmem_alloc(smem_u32(tmem_slot), G::TMEM_COLS);
@@ -159,7 +149,6 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), i * BK, m0);
                 tma_load_2d(smem_u32(stageW(s)), &tmW, full(s), i * BK, n0);
                 tma_load_2d(smem_u32(stageWlo(s)), &tmWlo, full(s), i * BK, n0);
-                if (ALO) tma_load_2d(smem_u32(stageAlo(s)), &tmAlo, full(s), i * BK, m0);
                 issued = i + 1;
             }
         }
@@ -168,79 +157,83 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             constexpr uint32_t idesc = idesc_tf32(BM, BN);
             for (int i = 0; i < nk && ok; ++i) {
                 const int s = i % S, b = i & 1;
-                if (!mbar_wait(ALO ? full(s) : conv(s), (i / S) & 1, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(conv(s), (i / S) & 1, abort_flag)) { ok = false; break; }
                 if (!mbar_wait(tdrain(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t acc = tmem + b * BN;
-                const uint32_t a = smem_u32(stageA(s)), alo = smem_u32(ALO ? stageAlo(s) : bufAlo(b));
+                const uint32_t acc = tmem + G::ACC_COL + b * BN;
+                const int ab = i % NAB;
+                const uint32_t ahi = tmem + G::A_COL + ab * 64, alo = ahi + 32;
                 const uint32_t w = smem_u32(stageW(s)), wlo = smem_u32(stageWlo(s));
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint32_t ko = kk * 32;  // 8 tf32 = 32 bytes along the swizzled row
-                    const uint64_t da = smem_desc_sw128(a + ko), dal = smem_desc_sw128(alo + ko);
-                    const uint64_t dw = smem_desc_sw128(w + ko), dwl = smem_desc_sw128(wlo + ko);
-                    mma_tf32(acc, dal, dw, idesc, kk != 0);
-                    mma_tf32(acc, da, dwl, idesc, 1);
-                    mma_tf32(acc, da, dw, idesc, 1);
+                    const uint64_t dw = smem_desc_sw128(w + kk * 32), dwl = smem_desc_sw128(wlo + kk * 32);
+                    mma_tf32_ts(acc, alo + kk * 8, dw, idesc, kk != 0);
+                    mma_tf32_ts(acc, ahi + kk * 8, dwl, idesc, 1);
+                    mma_tf32_ts(acc, ahi + kk * 8, dw, idesc, 1);
                 }
                 mma_commit(empty(s));
-                mma_commit(lofree(b));
+                mma_commit(afree(ab));
                 mma_commit(tfull(b));
             }
         }
-    } else if (warp < W_ACC0) {
-        if (ALO) goto done_roles;
-        const int tid = threadIdx.x - W_SPLIT0 * 32;
+    } else if (warp >= W_A0 && warp < W_A0 + 4) {
+        // A warps: warp (w % 4) owns TMEM lanes = tile rows 32*(w%4)..+31;
+        // each thread moves its row of the stage's A tile into TMEM as
+        // hi = tf32(a) and lo = a - hi
+        const int q = warp & 3, r = q * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::A_COL;
         for (int i = 0; i < nk && ok; ++i) {
-            const int s = i % S, b = i & 1;
+            const int s = i % S, b = i % NAB;
             if (!mbar_wait(full(s), (i / S) & 1, abort_flag)) { ok = false; break; }
-            if (!mbar_wait(lofree(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
-            split_lo(stageA(s), bufAlo(b), A_TILE, tid, (N_SPLIT + N_ACC) * 32);
-            fence_proxy_async_smem();
+            if (!mbar_wait(afree(b), ((i / NAB) & 1) ^ 1, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            const uint8_t *row = stageA(s) + r * 128;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t hi[16], lo[16];
+#pragma unroll
+                for (int c4 = 0; c4 < 4; ++c4) {
+                    const int c = hf * 4 + c4;
+                    const float4 v = *reinterpret_cast<const float4 *>(row + (((c ^ (r & 7))) << 4));
+                    const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float h = tf32_hi(x[u]);
+                        hi[c4 * 4 + u] = __float_as_uint(h);
+                        lo[c4 * 4 + u] = __float_as_uint(__fsub_rn(x[u], h));
+                    }
+                }
+                tmem_st_32x32b_x16(lane_base + b * 64 + hf * 16, hi);
+                tmem_st_32x32b_x16(lane_base + b * 64 + 32 + hf * 16, lo);
+            }
+            tmem_st_wait();
+            tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(conv(s));
         }
-    } else {
+    } else if (warp >= W_ACC0 && warp < W_ACC0 + NACC) {
         // accumulator / epilogue warps: warp w owns TMEM lanes 32*(w%4)..+31
-        // (tile rows) and one half of the tile's columns
-        constexpr int CPA = G::COLS_PER_ACC;
-        const int q = warp & 3, half = (warp - W_ACC0) >> 2;
-        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + half * CPA;
-        float acc[CPA];
+        // (tile rows) and one 64-column group of the tile
+        const int q = warp & 3, grp = (warp - W_ACC0) >> 2;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::ACC_COL + grp * 64;
+        float acc[64];
 #pragma unroll
-        for (int j = 0; j < CPA; ++j) acc[j] = 0.0f;
-        // per iteration: help split stage i (unless A_lo comes from HBM), then
-        // drain chunk i-1 -- the drain of a chunk never waits on a split the
-        // same warps still have to do
-        const int stid = N_SPLIT * 32 + (threadIdx.x - W_ACC0 * 32);
-        auto drain = [&](int i) {
+        for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+        for (int i = 0; i < nk && ok; ++i) {
             const int b = i & 1;
-            if (!mbar_wait(tfull(b), (i >> 1) & 1, abort_flag)) return false;
+            if (!mbar_wait(tfull(b), (i >> 1) & 1, abort_flag)) { ok = false; break; }
             tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < CPA / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(lane_base + b * BN + c * 32, r);
+            for (int c = 0; c < 4; ++c) {
+                uint32_t rr[16];
+                tmem_ld_32x32b_x16(lane_base + b * BN + c * 16, rr);
                 tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __fadd_rn(acc[c * 32 + j], __uint_as_float(r[j]));
+                for (int j = 0; j < 16; ++j) acc[c * 16 + j] = __fadd_rn(acc[c * 16 + j], __uint_as_float(rr[j]));
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tdrain(b));
-            return true;
-        };
-        for (int i = 0; i <= nk && ok; ++i) {
-            if (!ALO && i < nk) {
-                const int s = i % S, b = i & 1;
-                if (!mbar_wait(full(s), (i / S) & 1, abort_flag) ||
-                    !mbar_wait(lofree(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                split_lo(stageA(s), bufAlo(b), A_TILE, stid, (N_SPLIT + N_ACC) * 32);
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(conv(s));
-            }
-            if (i > 0 && !drain(i - 1)) { ok = false; break; }
         }
         // epilogue: raw sums staged row-major in the (now idle) stage buffers,
         // then one pass that applies alpha, bias and the activation and writes
@@ -248,37 +241,33 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         // per-element unrolled epilogue with Erf-GELU inlined overflows the
         // instruction cache).
         constexpr int PITCH = BN + 4;  // floats; keeps the per-row writes conflict-free
-        static_assert(BM * PITCH * 4 <= G::STAGES * G::STAGE, "C tile must fit in the stage ring");
-        float *ctile = reinterpret_cast<float *>(smem);
-        float *sbias = ctile + BM * PITCH;  // BN floats
         static_assert(BM * PITCH * 4 + BN * 4 <= G::STAGES * G::STAGE, "C tile + bias must fit in the stage ring");
-        const int rloc = q * 32 + lane;
-        {
-            const int t = threadIdx.x - W_ACC0 * 32;
-            for (int c = t; c < BN; c += N_ACC * 32) {
-                const int col = n0 + c;
-                float bv = 0.0f;
-                if (bias && col < N) bv = beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col));
-                sbias[c] = bv;
-            }
+        float *ctile = reinterpret_cast<float *>(smem);
+        float *sbias = ctile + BM * PITCH;
+        const int t = threadIdx.x - W_ACC0 * 32;
+        for (int c = t; c < BN; c += NACC * 32) {
+            const int col = n0 + c;
+            float bv = 0.0f;
+            if (bias && col < N) bv = beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col));
+            sbias[c] = bv;
         }
+        const int rloc = q * 32 + lane;
         if (ok) {
 #pragma unroll
-            for (int j = 0; j < CPA; j += 4)
-                *reinterpret_cast<float4 *>(ctile + rloc * PITCH + half * CPA + j) =
+            for (int j = 0; j < 64; j += 4)
+                *reinterpret_cast<float4 *>(ctile + rloc * PITCH + grp * 64 + j) =
                     make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
         }
-        asm volatile("bar.sync 1, %0;" ::"n"(N_ACC * 32) : "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
         if (ok) {
-            const int t = threadIdx.x - W_ACC0 * 32;
             constexpr int V4 = BN / 4;  // float4 per tile row
             const bool vec = (ldc & 3) == 0 && n0 + BN <= N;
 #pragma unroll 1
-            for (int e = t; e < BM * V4; e += N_ACC * 32) {
-                const int r = e / V4, c4 = e % V4;
-                const int grow = m0 + r;
+            for (int e = t; e < BM * V4; e += NACC * 32) {
+                const int rr = e / V4, c4 = e % V4;
+                const int grow = m0 + rr;
                 if (grow >= M) continue;
-                const float4 raw = *reinterpret_cast<const float4 *>(ctile + r * PITCH + c4 * 4);
+                const float4 raw = *reinterpret_cast<const float4 *>(ctile + rr * PITCH + c4 * 4);
                 float v[4] = {raw.x, raw.y, raw.z, raw.w};
                 const int col0 = n0 + c4 * 4;
 #pragma unroll
@@ -301,7 +290,6 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         }
     }
 
-done_roles:
     if (!ok) {
         *abort_flag = 1;
         atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
@@ -324,16 +312,6 @@ done_roles:
     if (warp == W_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem, G::TMEM_COLS);
-    }
-}
-
-// Activation low parts: lo = a - tf32(a), row-major like a (fp32 streaming).
-__global__ void k_split_lo(const float4 *__restrict__ a, float4 *__restrict__ lo, int64_t n4) {
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
-        const float4 v = __ldg(a + i);
-        lo[i] = make_float4(__fsub_rn(v.x, tf32_hi(v.x)), __fsub_rn(v.y, tf32_hi(v.y)), __fsub_rn(v.z, tf32_hi(v.z)),
-                            __fsub_rn(v.w, tf32_hi(v.w)));
     }
 }
 
@@ -389,19 +367,18 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
     return LONNX_OK;
 }
 
-template <int BN, bool ALO>
-int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &malo, const CUtensorMap &mw,
-              const CUtensorMap &mwlo, const float *bias, float *C, int M, int N, int K, int ldc, float alpha,
-              float beta, int epi) {
-    using G = Cfg<BN, ALO>;
+template <int BN>
+int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, const CUtensorMap &mwlo,
+              const float *bias, float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi) {
+    using G = Cfg<BN>;
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {
-        LONNX_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, ALO>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
+        LONNX_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
         attr_set[ctx->device & 63] = true;
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-    k_gemm_tf32x3<BN, ALO><<<grid, kThreads, G::SMEM, ctx->stream>>>(ma, malo, mw, mwlo, bias, C, M, N, K, ldc, alpha,
-                                                                     beta, epi, ctx->dev_flags);
+    k_gemm_tf32x3<BN><<<grid, kThreads, G::SMEM, ctx->stream>>>(ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi,
+                                                                ctx->dev_flags);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
 }
@@ -409,6 +386,11 @@ int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &malo, co
 // Tile width for N: 192 or 128, whichever divides N, else the one with the
 // least padding.
 int pick_bn(int N) {
+    static const int forced = [] {
+        const char *e = getenv("LONNX_GEMM_BN");
+        return e ? atoi(e) : 0;
+    }();
+    if (forced == 128 || forced == 192) return forced;
     if (N % 192 == 0) return 192;
     if (N % 128 == 0) return 128;
     return ((N + 191) / 192 * 192 - N) < ((N + 127) / 128 * 128 - N) ? 192 : 128;
@@ -432,32 +414,9 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
     if (rc) return rc;
     rc = make_map(&mwlo, Wlo, N, K, ldw, bn);
     if (rc) return rc;
-    // A's low parts: split inside the kernel per tile (default; measured
-    // faster on every BASELINE shape), or streamed once into scratch and
-    // TMA-loaded beside A (LONNX_GEMM_ALO=1).
-    static const int mode = [] {
-        const char *e = getenv("LONNX_GEMM_ALO");
-        return e ? atoi(e) : -1;
-    }();
-    const bool alo = mode > 0;
-    if (alo && allow_scratch) {
-        // A_lo streamed into scratch, then TMA-loaded beside A
-        void *tmp = nullptr;
-        rc = ctx_scratch2(ctx, (size_t)M * lda * 4, &tmp);
-        if (rc) return rc;
-        const int64_t n4 = (int64_t)M * lda / 4;
-        int64_t blocks = (n4 + 255) / 256;
-        if (blocks > (int64_t)ctx->num_sms * 16) blocks = (int64_t)ctx->num_sms * 16;
-        k_split_lo<<<(int)blocks, 256, 0, ctx->stream>>>((const float4 *)A, (float4 *)tmp, n4);
-        LONNX_CHECK_LAUNCH(ctx);
-        CUtensorMap malo;
-        rc = make_map(&malo, (const float *)tmp, M, K, lda, BM);
-        if (rc) return rc;
-        if (bn == 192) return launch_tc<192, true>(ctx, ma, malo, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
-        return launch_tc<128, true>(ctx, ma, malo, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
-    }
-    if (bn == 192) return launch_tc<192, false>(ctx, ma, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
-    return launch_tc<128, false>(ctx, ma, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
+    (void)allow_scratch;  // this path allocates nothing
+    if (bn == 192) return launch_tc<192>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
+    return launch_tc<128>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
 }
 
 int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans) {
