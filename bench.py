@@ -126,7 +126,7 @@ def gemm_roofline(ctx, st, torch, M=32768, K=384, N=1536, reps=20):
             "peak": tf32_peak, "unit": "TFLOP/s", "frac": round(achieved / tf32_peak, 4),
             "peak_note": f"dense tf32 = {kind} bf16 / 2; achieved counts algorithmic fp32 FLOPs (2MNK); "
                          "3xTF32 issues 3 tf32 MMAs per product, so tensor-pipe use is 3x frac",
-            "traffic": None}
+            "traffic": _ncu_traffic()}
 
 
 def _oracle_graph():
@@ -134,6 +134,16 @@ def _oracle_graph():
     g = G.e5_encoder(vocab=250037, seq=SEQ, seed=0)
     g.outputs = ["sentence_embedding"]
     return g
+
+
+def _ncu_traffic():
+    """DRAM bytes per launch of the roofline GEMM from the committed ncu
+    capture (profiles/gemm_tf32x3_ffn1_roofline.json), or None."""
+    p = os.path.join(ROOT, "profiles", "gemm_tf32x3_ffn1_roofline.json")
+    try:
+        return json.load(open(p))["dram_bytes_per_launch"]
+    except (OSError, KeyError, ValueError):
+        return None
 
 
 def cpu_baseline(n_seq=8, g=None):
@@ -259,11 +269,19 @@ def main():
     ap.add_argument("--vocab", type=int, default=250037)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-resnet", action="store_true")
+    ap.add_argument("--roofline-case", action="store_true",
+                    help="run only the roofline GEMM (FFN1 shape) and exit (for ncu captures)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="B",
                     help="run two 2-layer e5 forwards at batch B and exit (small case for ncu captures)")
     args = ap.parse_args()
     if args.profile_case:
         return profile_case(args.profile_case)
+    if args.roofline_case:
+        import torch
+        from onnx_b200.tensor import Context
+        ctx = Context(0)
+        print(json.dumps(gemm_roofline(ctx, torch.cuda.ExternalStream(ctx.stream), torch, reps=3)))
+        return
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
