@@ -64,6 +64,11 @@ LONNX_API int lonnx_memcpy_d2d(lonnx_ctx *ctx, void *dst, const void *src, size_
 LONNX_API int lonnx_memset(lonnx_ctx *ctx, void *dst, int value, size_t bytes);
 LONNX_API int lonnx_sync(lonnx_ctx *ctx);
 LONNX_API const char *lonnx_last_error(void);
+/* Failure-detection test hook: enqueue a kernel whose bounded device wait
+ * (on a word nothing sets) expires after `cycles` SM clocks; the next
+ * lonnx_sync() returns LONNX_E_TIMEOUT and the context stays usable.  Same
+ * reporting path as an expired pipeline wait in the tensor-core kernels. */
+LONNX_API int lonnx_debug_expire_wait(lonnx_ctx *ctx, int64_t cycles);
 /* Count of this library's kernel launches on ctx since creation. */
 LONNX_API int64_t lonnx_launch_count(const lonnx_ctx *ctx);
 

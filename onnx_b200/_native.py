@@ -35,6 +35,7 @@ _SIGS = {
     "lonnx_sync": (c_int, [c_vp]),
     "lonnx_last_error": (c_char_p, []),
     "lonnx_launch_count": (c_i64, [c_vp]),
+    "lonnx_debug_expire_wait": (c_int, [c_vp, c_i64]),
     "lonnx_broadcast_shape": (c_int, [i64p, c_int, i64p, c_int, i64p, ctypes.POINTER(c_int)]),
     "lonnx_binary_f32": (c_int, [c_vp, c_int, c_vp, i64p, c_int, c_vp, i64p, c_int, c_vp]),
     "lonnx_unary_f32": (c_int, [c_vp, c_int, c_vp, c_vp, c_i64]),

@@ -246,4 +246,28 @@ LONNX_API int lonnx_sync(lonnx_ctx *ctx) {
     return LONNX_OK;
 }
 
+// Test hook for failure detection: one thread waits on a device word that
+// nothing sets, gives up after `cycles` SM clocks (a bounded wait, like every
+// pipeline wait in this library), records LONNX_E_TIMEOUT in the context's
+// flags and returns.  The kernel always terminates; the context stays usable.
+static __global__ void k_expire_wait(const volatile int *never, int *flags, long long cycles) {
+    const long long t0 = clock64();
+    while (*never == 0) {
+        if (clock64() - t0 > cycles) {
+            atomicExch(flags + lonnx::FLAG_TIMEOUT, 2);
+            return;
+        }
+    }
+}
+
+LONNX_API int lonnx_debug_expire_wait(lonnx_ctx *ctx, int64_t cycles) {
+    int rc = device_guard(ctx);
+    if (rc) return rc;
+    if (cycles <= 0 || cycles > 4000000000ll) return set_error(LONNX_E_BADARG, "cycles out of range");
+    // flags[FLAG_COUNT-1] is never written by the library: the word nothing sets
+    k_expire_wait<<<1, 1, 0, ctx->stream>>>(ctx->dev_flags + FLAG_COUNT - 1, ctx->dev_flags, cycles);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
 }  // extern "C"

@@ -127,3 +127,43 @@ def test_sharded_replicas_gloo_world2():
     g = G.e5_encoder(layers=1, vocab=300, seq=8, seed=4)
     ref = O.execute(g, G.e5_inputs(5, 8, 300, seed=4))["sentence_embedding"]
     assert np.array_equal(got, ref)
+
+
+def _rank_fail_main(rank, world, port, q):
+    import datetime
+    import os as _os
+    import sys
+    sys.path.insert(0, ROOT)
+    _os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    from onnx_b200.shard import run_sharded
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+
+    def execute(x):
+        if rank == 1:
+            raise RuntimeError("injected failure on rank 1")
+        return {"y": x["x"] * 2}
+    try:
+        run_sharded(execute, {"x": np.arange(6, dtype=np.float32).reshape(6, 1)})
+        q.put((rank, "finished"))
+    except Exception as e:  # rank 1: its own exception; rank 0: the gather times out / sees the peer gone
+        q.put((rank, type(e).__name__))
+
+
+def test_sharded_rank_failure_is_detected_gloo():
+    """A rank that fails between steps: the other rank's host-side gather ends
+    with an error (process-group timeout or peer loss) instead of hanging."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_fail_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=90) for _ in range(2))
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "RuntimeError"
+    assert res[0] != "finished"
