@@ -87,6 +87,37 @@ k_gemm_simt(const float *__restrict__ A, const float *__restrict__ B, const floa
     }
 }
 
+// Tiny outputs (e.g. the mnist-8 classifier, 1 x 256 . 256 x 10): one thread
+// per output element, sequential over k with a separate multiply and add --
+// the same order as k_gemm_simt, without its tile loop and block barriers,
+// which make a one-block launch latency-bound.
+template <bool TB>
+__global__ void k_gemm_rowdot(const float *__restrict__ A, const float *__restrict__ B, const float *__restrict__ bias,
+                              const float *__restrict__ res, float *__restrict__ C, int M, int N, int K, int64_t sA,
+                              int64_t sB, int64_t sC, int batch, float alpha, float beta, int epi) {
+    const int64_t total = (int64_t)batch * M * N;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int n = (int)(t % N);
+        const int m = (int)((t / N) % M);
+        const int b = (int)(t / ((int64_t)N * M));
+        const float *a = A + b * sA + (int64_t)m * K;
+        const float *bb = B + b * sB;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int k = 0; k < K; ++k) {
+            const float bv = TB ? __ldg(bb + (int64_t)n * K + k) : __ldg(bb + (int64_t)k * N + n);
+            acc = __fadd_rn(acc, __fmul_rn(__ldg(a + k), bv));
+        }
+        float v = acc;
+        if (alpha != 1.0f) v = __fmul_rn(v, alpha);
+        if (bias) v = __fadd_rn(v, beta == 1.0f ? bias[n] : __fmul_rn(beta, bias[n]));
+        if (res) v = __fadd_rn(v, res[b * sC + (int64_t)m * N + n]);
+        if (epi == LONNX_EPI_RELU) v = v > 0.0f ? v : 0.0f;
+        else if (epi == LONNX_EPI_GELU_ERF) v = lonnx_gelu_chain(v);
+        C[b * sC + (int64_t)m * N + n] = v;
+    }
+}
+
 // Direct NCHW convolution, one thread per output element, summing over
 // (c, ky, kx) in the im2col row order of MathOps.Conv2D with a separate
 // multiply and add (MathOps.cs:821-846), then the bias pass (:862-872) and
@@ -181,6 +212,18 @@ int transpose_launch(lonnx_ctx *ctx, const void *x, int elem_bytes, const int64_
 int gemm_simt(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
               int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
               float alpha, float beta, int epi, const float *residual) {
+    if ((int64_t)batch * M * N <= 16384) {
+        const int64_t total = (int64_t)batch * M * N;
+        const int blocks = (int)((total + 127) / 128);
+        if (transB)
+            k_gemm_rowdot<true><<<blocks, 128, 0, ctx->stream>>>(A, B, bias, residual, C, M, N, K, sA, sB, sC, batch,
+                                                                 alpha, beta, epi);
+        else
+            k_gemm_rowdot<false><<<blocks, 128, 0, ctx->stream>>>(A, B, bias, residual, C, M, N, K, sA, sB, sC, batch,
+                                                                  alpha, beta, epi);
+        LONNX_CHECK_LAUNCH(ctx);
+        return LONNX_OK;
+    }
     dim3 grid((N + SB_N - 1) / SB_N, (M + SB_M - 1) / SB_M, batch);
     if (grid.z > 65535) return set_error(LONNX_E_UNSUPPORTED, "gemm: batch %d too large", batch);
     if (transB)
