@@ -269,6 +269,8 @@ def main():
     ap.add_argument("--vocab", type=int, default=250037)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-resnet", action="store_true")
+    ap.add_argument("--resnet-case", type=int, default=0, metavar="B",
+                    help="run only the ResNet-50 forward at batch B and exit (for profiler captures)")
     ap.add_argument("--roofline-case", action="store_true",
                     help="run only the roofline GEMM (FFN1 shape) and exit (for ncu captures)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="B",
@@ -276,6 +278,13 @@ def main():
     args = ap.parse_args()
     if args.profile_case:
         return profile_case(args.profile_case)
+    if args.resnet_case:
+        import torch
+        from onnx_b200.tensor import Context
+        ctx = Context(0)
+        print(json.dumps(resnet_throughput(ctx, torch.cuda.ExternalStream(ctx.stream), torch, batch=args.resnet_case,
+                                           reps=2)))
+        return
     if args.roofline_case:
         import torch
         from onnx_b200.tensor import Context

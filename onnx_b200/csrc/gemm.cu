@@ -154,29 +154,6 @@ __global__ void k_conv2d_direct(const float *__restrict__ x, const float *__rest
     }
 }
 
-// im2col in row-per-output-pixel form for the tensor-core conv:
-// col[(n, oy, ox), k] with k = (c, ky, kx) in the reference's im2col row order
-// (MathOps.cs:654-709), K padded with zeros to ldk (a multiple of 4, for TMA).
-__global__ void k_im2col_rows(const float *__restrict__ x, float *__restrict__ col, int N, int C, int H, int W,
-                              int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw, int Ho, int Wo, int K,
-                              int ldk) {
-    const int64_t total = (int64_t)N * Ho * Wo * ldk;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += stride) {
-        const int k = (int)(t % ldk);
-        const int64_t pix = t / ldk;
-        float v = 0.0f;
-        if (k < K) {
-            const int ox = (int)(pix % Wo), oy = (int)((pix / Wo) % Ho);
-            const int n = (int)(pix / ((int64_t)Wo * Ho));
-            const int kx = k % kw, ky = (k / kw) % kh, c = k / (kw * kh);
-            const int iy = oy * sh - pt + ky * dh, ix = ox * sw - pl + kx * dw;
-            if (iy >= 0 && iy < H && ix >= 0 && ix < W) v = __ldg(x + (((int64_t)n * C + c) * H + iy) * W + ix);
-        }
-        col[t] = v;
-    }
-}
-
 // weight [M, K] -> hi, lo [M, ldk] (tf32 split, zero padded)
 __global__ void k_split_pad_rows(const float *__restrict__ w, float *__restrict__ hi, float *__restrict__ lo, int M,
                                  int K, int ldk) {
@@ -189,6 +166,16 @@ __global__ void k_split_pad_rows(const float *__restrict__ w, float *__restrict_
         const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
         hi[t] = h;
         lo[t] = __fsub_rn(v, h);
+    }
+}
+
+// y = y + r (then ReLU): a Conv -> Add [-> Relu] chain off the tensor cores
+__global__ void k_add_relu(float *__restrict__ y, const float *__restrict__ r, int64_t n, int relu) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += stride) {
+        float v = __fadd_rn(y[t], r[t]);
+        if (relu) v = v > 0.0f ? v : 0.0f;
+        y[t] = v;
     }
 }
 
@@ -374,6 +361,23 @@ LONNX_API int lonnx_conv2d_f32(lonnx_ctx *ctx, const float *x, const float *w, c
                                int relu) {
     int rc = device_guard(ctx);
     if (rc) return rc;
+    return lonnx::conv2d(ctx, x, w, nullptr, nullptr, bias, nullptr, y, N, C, H, W, M, kh, kw, sh, sw, pt, pl, pb, pr,
+                         dh, dw, group, relu);
+}
+
+}  // extern "C"
+
+namespace lonnx {
+
+int split_pad_rows(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int M, int K, int ldk) {
+    k_split_pad_rows<<<grid_for(ctx, (int64_t)M * ldk), 256, 0, ctx->stream>>>(w, hi, lo, M, K, ldk);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, const float *wlo, const float *bias,
+           const float *res, float *y, int N, int C, int H, int W, int M, int kh, int kw, int sh, int sw, int pt,
+           int pl, int pb, int pr, int dh, int dw, int group, int relu) {
     if (!x || !w || !y || N < 0 || C <= 0 || M <= 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 ||
         dh <= 0 || dw <= 0 || group <= 0 || C % group || M % group)
         return set_error(LONNX_E_BADARG, "conv2d: bad arguments");
@@ -383,42 +387,42 @@ LONNX_API int lonnx_conv2d_f32(lonnx_ctx *ctx, const float *x, const float *w, c
     const int64_t total = (int64_t)N * M * Ho * Wo;
     if (total == 0) return LONNX_OK;
     const int K = C * kh * kw;
+    const int64_t P = (int64_t)N * Ho * Wo;
     static const bool tc_off = getenv("LONNX_DISABLE_TC") != nullptr;
-    if (!tc_off && group == 1 && total * K >= gemm_tc_min_work()) {
-        // GEMM formulation on the tensor cores: rows = output pixels (N*Ho*Wo),
-        // cols = output channels, contraction over (c, ky, kx); per-channel
-        // bias and ReLU in the GEMM epilogue; NHWC result -> NCHW.
+    if (!tc_off && group == 1 && total * K >= gemm_tc_min_work() && P < (1ll << 31) &&
+        (int64_t)N * C * H * W < (1ll << 40)) {
+        // implicit GEMM on the tensor cores: rows = output pixels (N*Ho*Wo),
+        // columns = output channels, contraction over (c, ky, kx) in the
+        // reference's im2col order; input gathered inside the kernel, bias,
+        // residual and ReLU in the epilogue, NCHW written directly
         const int ldk = (K + 3) & ~3;
-        const int64_t P = (int64_t)N * Ho * Wo;
-        void *col = nullptr, *wt = nullptr, *tmp = nullptr;
-        rc = ctx_alloc(ctx, (size_t)P * ldk * 4, &col);
-        if (rc) return rc;
-        rc = ctx_alloc(ctx, (size_t)2 * M * ldk * 4, &wt);
-        if (rc) { ctx_free(ctx, col); return rc; }
-        rc = ctx_alloc(ctx, (size_t)P * M * 4, &tmp);
-        if (rc) { ctx_free(ctx, col); ctx_free(ctx, wt); return rc; }
-        k_im2col_rows<<<grid_for(ctx, P * ldk), 256, 0, ctx->stream>>>(x, (float *)col, N, C, H, W, kh, kw, sh, sw, pt,
-                                                                       pl, dh, dw, Ho, Wo, K, ldk);
-        LONNX_CHECK_LAUNCH(ctx);
-        float *whi = (float *)wt, *wlo = whi + (size_t)M * ldk;
-        k_split_pad_rows<<<grid_for(ctx, (int64_t)M * ldk), 256, 0, ctx->stream>>>(w, whi, wlo, M, K, ldk);
-        LONNX_CHECK_LAUNCH(ctx);
-        rc = P < (1ll << 31) ? gemm_tc(ctx, (const float *)col, whi, wlo, bias, (float *)tmp, (int)P, M, ldk, ldk, ldk,
-                                       M, 1.0f, 1.0f, relu ? LONNX_EPI_RELU : LONNX_EPI_NONE)
-                             : LONNX_E_UNSUPPORTED;
-        if (rc == LONNX_OK) {
-            const int64_t shp[3] = {N, (int64_t)Ho * Wo, M}, perm[3] = {0, 2, 1};
-            rc = transpose_launch(ctx, tmp, 4, shp, 3, perm, y);
+        void *wt = nullptr;
+        if (!whi || !wlo) {
+            int rc = ctx_alloc(ctx, (size_t)2 * M * ldk * 4, &wt);
+            if (rc) return rc;
+            whi = (const float *)wt;
+            wlo = whi + (size_t)M * ldk;
+            rc = split_pad_rows(ctx, w, (float *)whi, (float *)wlo, M, K, ldk);
+            if (rc) { ctx_free(ctx, wt); return rc; }
         }
-        ctx_free(ctx, col);
-        ctx_free(ctx, wt);
-        ctx_free(ctx, tmp);
+        ConvArgs cv;
+        cv.x = x;
+        cv.C = C; cv.H = H; cv.W = W; cv.kh = kh; cv.kw = kw; cv.sh = sh; cv.sw = sw;
+        cv.pt = pt; cv.pl = pl; cv.dh = dh; cv.dw = dw; cv.Ho = Ho; cv.Wo = Wo;
+        cv.img_rows = Ho * Wo;
+        cv.res = res;
+        int rc = conv_tc(ctx, cv, whi, wlo, ldk, bias, y, (int)P, M, K, relu ? LONNX_EPI_RELU : LONNX_EPI_NONE);
+        if (wt) ctx_free(ctx, wt);
         if (rc != LONNX_E_UNSUPPORTED) return rc;
     }
     k_conv2d_direct<<<grid_for(ctx, total), 256, 0, ctx->stream>>>(x, w, bias, y, N, C, H, W, M, kh, kw, sh, sw, pt,
-                                                                     pl, dh, dw, group, Ho, Wo, relu);
+                                                                     pl, dh, dw, group, Ho, Wo, res ? 0 : relu);
     LONNX_CHECK_LAUNCH(ctx);
+    if (res) {
+        k_add_relu<<<grid_for(ctx, total), 256, 0, ctx->stream>>>(y, res, total, relu);
+        LONNX_CHECK_LAUNCH(ctx);
+    }
     return LONNX_OK;
 }
 
-}  // extern "C"
+}  // namespace lonnx

@@ -82,7 +82,8 @@ template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
               const __grid_constant__ CUtensorMap tmWlo, const float *__restrict__ bias, float *__restrict__ C,
-              int M, int N, int K, int ldc, float alpha, float beta, int epi, int *dev_flags) {
+              int M, int N, int K, int ldc, float alpha, float beta, int epi, int *dev_flags,
+              const lonnx::ConvArgs cv) {
     using G = Cfg<BN>;
     constexpr int S = G::STAGES;
     constexpr int NACC = 4 * G::GROUPS;  // accumulator warps in use
@@ -141,12 +142,12 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
 
     if (warp == W_TMA) {
         if (lane == 0) {
-            constexpr uint32_t bytes = G::STAGE;
+            const uint32_t bytes = cv.x ? 2 * G::W_TILE : G::STAGE;
             for (int i = 0; i < nk && ok; ++i) {
                 const int s = i % S;
                 if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 mbar_arrive_expect_tx(full(s), bytes);
-                tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), i * BK, m0);
+                if (!cv.x) tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), i * BK, m0);
                 tma_load_2d(smem_u32(stageW(s)), &tmW, full(s), i * BK, n0);
                 tma_load_2d(smem_u32(stageWlo(s)), &tmWlo, full(s), i * BK, n0);
                 issued = i + 1;
@@ -158,6 +159,8 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             for (int i = 0; i < nk && ok; ++i) {
                 const int s = i % S, b = i & 1;
                 if (!mbar_wait(conv(s), (i / S) & 1, abort_flag)) { ok = false; break; }
+                // implicit conv: the A warps do not wait for the W tiles, so the MMA does
+                if (cv.x && !mbar_wait(full(s), (i / S) & 1, abort_flag)) { ok = false; break; }
                 if (!mbar_wait(tdrain(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t acc = tmem + G::ACC_COL + b * BN;
@@ -182,7 +185,78 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         // hi = tf32(a) and lo = a - hi
         const int q = warp & 3, r = q * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::A_COL;
-        for (int i = 0; i < nk && ok; ++i) {
+        if (cv.x) {
+            // implicit-GEMM conv: row r is output pixel m0 + r, column k is
+            // (c, ky, kx).  Each thread gathers its pixel's 32 taps of a
+            // stage straight from the NCHW input with 4-byte cp.async into
+            // its own row of the stage's (otherwise unused) A slot, S - 1
+            // stages ahead; lanes are consecutive pixels, so each tap is one
+            // coalesced warp access; taps outside the image or past K are
+            // zero-filled.  Rows are rotated by r words so the 32 lanes hit
+            // 32 banks.
+            constexpr int D = S - 1;
+            int iy0 = -(1 << 20), ix0 = 0;
+            const float *xr = cv.x;
+            const int p = m0 + r;
+            if (p < M) {
+                const int hw = cv.Ho * cv.Wo, n = p / hw, rem = p - n * hw;
+                const int oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
+                iy0 = oy * cv.sh - cv.pt;
+                ix0 = ox * cv.sw - cv.pl;
+                xr = cv.x + (int64_t)n * cv.C * cv.H * cv.W + (int64_t)iy0 * cv.W + ix0;
+            }
+            const int khw = cv.kh * cv.kw, HW = cv.H * cv.W;
+            auto gather = [&](int i) {
+                const uint32_t row = smem_u32(stageA(i % S)) + r * 128;
+                const int k = i * BK + lane;
+                int off = 0, dy = -(1 << 20), dx = 0;  // taps past K read as zero
+                if (k < K) {
+                    const int c = k / khw, rr = k - c * khw, ky = rr / cv.kw, kx = rr - ky * cv.kw;
+                    dy = ky * cv.dh;
+                    dx = kx * cv.dw;
+                    off = c * HW + dy * cv.W + dx;
+                }
+#pragma unroll 4
+                for (int u = 0; u < BK; ++u) {
+                    const int o = __shfl_sync(0xffffffffu, off, u);
+                    const int yy = iy0 + __shfl_sync(0xffffffffu, dy, u);
+                    const int xx = ix0 + __shfl_sync(0xffffffffu, dx, u);
+                    const bool in = (unsigned)yy < (unsigned)cv.H && (unsigned)xx < (unsigned)cv.W;
+                    cp_async4(row + (((u + r) & 31) << 2), in ? xr + o : cv.x, in ? 4u : 0u);
+                }
+            };
+            for (int j = 0; j < D; ++j) {
+                if (j < nk) gather(j);
+                cp_async_commit();
+            }
+            for (int i = 0; i < nk && ok; ++i) {
+                const int s = i % S, b = i % NAB;
+                if (i + D < nk) gather(i + D);
+                cp_async_commit();
+                cp_async_wait<D>();  // this thread's taps of stage i have landed
+                const float *row = reinterpret_cast<const float *>(stageA(s) + r * 128);
+                if (!mbar_wait(afree(b), ((i / NAB) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint32_t hi[16], lo[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float x = row[(hf * 16 + j + r) & 31], h = tf32_hi(x);
+                        hi[j] = __float_as_uint(h);
+                        lo[j] = __float_as_uint(__fsub_rn(x, h));
+                    }
+                    tmem_st_32x32b_x16(lane_base + b * 64 + hf * 16, hi);
+                    tmem_st_32x32b_x16(lane_base + b * 64 + 32 + hf * 16, lo);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(conv(s));
+            }
+            cp_async_wait<0>();
+        }
+        for (int i = 0; i < nk && ok && !cv.x; ++i) {
             const int s = i % S, b = i % NAB;
             if (!mbar_wait(full(s), (i / S) & 1, abort_flag)) { ok = false; break; }
             if (!mbar_wait(afree(b), ((i / NAB) & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -252,6 +326,43 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             sbias[c] = bv;
         }
         const int rloc = q * 32 + lane;
+        if (cv.img_rows > 0) {
+            // NCHW output: row = (image, pixel), column = channel; a warp's
+            // lanes hold consecutive pixels, so each column store coalesces.
+            // Optional residual (same layout) added after the bias, before
+            // the activation, as a following Add node would.
+            asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
+            const int grow = m0 + rloc;
+            if (ok && grow < M) {
+                const int img = grow / cv.img_rows, pix = grow - img * cv.img_rows;
+                const int64_t o = (int64_t)img * N * cv.img_rows + pix;
+                float *dst = C + o;
+                const float *rs = cv.res ? cv.res + o : nullptr;
+                const int cs = cv.img_rows;  // N * img_rows (one image's output) < 2^31
+#pragma unroll
+                for (int j0 = 0; j0 < 64; j0 += 8) {
+                    // residual loads for 8 columns first (all in flight at once)
+                    float rv[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int col = min(n0 + grp * 64 + j0 + j, N - 1);
+                        rv[j] = rs ? __ldg(rs + col * cs) : 0.0f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int cl = grp * 64 + j0 + j, col = n0 + cl;
+                        if (col < N) {
+                            float x = acc[j0 + j];
+                            if (alpha != 1.0f) x = __fmul_rn(x, alpha);
+                            if (bias) x = __fadd_rn(x, sbias[cl]);
+                            if (rs) x = __fadd_rn(x, rv[j]);
+                            if (epi == LONNX_EPI_RELU) x = x > 0.0f ? x : 0.0f;
+                            dst[col * cs] = x;
+                        }
+                    }
+                }
+            }
+        } else {
         if (ok) {
 #pragma unroll
             for (int j = 0; j < 64; j += 4)
@@ -287,6 +398,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                         if (col0 + u < N) dst[u] = v[u];
                 }
             }
+        }
         }
     }
 
@@ -369,7 +481,8 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
 
 template <int BN>
 int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, const CUtensorMap &mwlo,
-              const float *bias, float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi) {
+              const float *bias, float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi,
+              const lonnx::ConvArgs &cv) {
     using G = Cfg<BN>;
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {
@@ -378,7 +491,7 @@ int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, cons
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
     k_gemm_tf32x3<BN><<<grid, kThreads, G::SMEM, ctx->stream>>>(ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi,
-                                                                ctx->dev_flags);
+                                                                ctx->dev_flags, cv);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
 }
@@ -415,8 +528,27 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
     rc = make_map(&mwlo, Wlo, N, K, ldw, bn);
     if (rc) return rc;
     (void)allow_scratch;  // this path allocates nothing
-    if (bn == 192) return launch_tc<192>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
-    return launch_tc<128>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi);
+    const ConvArgs none{};
+    if (bn == 192) return launch_tc<192>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
+    return launch_tc<128>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
+}
+
+int conv_tc(lonnx_ctx *ctx, const ConvArgs &cv, const float *Whi, const float *Wlo, int ldw, const float *bias,
+            float *y, int P, int M, int K, int epi) {
+    auto al16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+    if (P <= 0 || M <= 0 || K <= 0 || (ldw & 3) || !al16(Whi) || !al16(Wlo) || !cv.x || cv.img_rows <= 0 ||
+        (epi != LONNX_EPI_NONE && epi != LONNX_EPI_RELU) || (int64_t)M * cv.img_rows >= (1ll << 31) ||
+        (int64_t)cv.C * cv.H * cv.W >= (1ll << 31))
+        return set_error(LONNX_E_UNSUPPORTED, "conv_tc: unsupported operands");
+    const int bn = pick_bn(M);
+    CUtensorMap mw, mwlo;
+    int rc = make_map(&mw, Whi, M, K, ldw, bn);
+    if (rc) return rc;
+    rc = make_map(&mwlo, Wlo, M, K, ldw, bn);
+    if (rc) return rc;
+    // the A map is unused in implicit mode (the kernel gathers A itself)
+    if (bn == 192) return launch_tc<192>(ctx, mw, mw, mwlo, bias, y, P, M, K, 0, 1.0f, 1.0f, epi, cv);
+    return launch_tc<128>(ctx, mw, mw, mwlo, bias, y, P, M, K, 0, 1.0f, 1.0f, epi, cv);
 }
 
 int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans) {

@@ -120,7 +120,7 @@ struct NodeDef {
     }
 };
 
-enum StepKind { S_NODE, S_GEMM, S_LN, S_ATTN, S_CONV_RELU };
+enum StepKind { S_NODE, S_GEMM, S_LN, S_ATTN, S_CONV };
 
 struct Step {
     StepKind kind = S_NODE;
@@ -365,7 +365,11 @@ void exec_matmul(lonnx_graph *g, const NodeDef &n) {
     g->env[n.out.at(0)] = y;
 }
 
-void exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string *out_name = nullptr) {
+// Conv node, optionally fused: relu = a following Relu, res = the other
+// input of a following Add (same shape as the Conv output; the caller
+// checks), whi/wlo = the weight split at prepare time.
+bool exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string *out_name = nullptr,
+               const Value *res = nullptr, const float *whi = nullptr, const float *wlo = nullptr) {
     Value x = lookup(g, n.in.at(0)), w = lookup(g, n.in.at(1));
     Value bias;
     const bool has_bias = n.in.size() > 2 && !n.in[2].empty();
@@ -408,10 +412,13 @@ void exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string
     ensure_dev(g, w);
     if (has_bias) ensure_dev(g, bias);
     Value y = new_dev(g, DT_FLOAT, {N, M, Ho, Wo});
-    ck(lonnx_conv2d_f32(g->ctx, (const float *)x.dptr(), (const float *)w.dptr(), has_bias ? (const float *)bias.dptr() : nullptr,
-                        (float *)y.dptr_mut(), N, C, H, W, M, kh, kw, (int)strides[0], (int)strides[1], pt, pl, pb, pr,
-                        (int)dil[0], (int)dil[1], group, relu));
+    if (res && res->shape != y.shape) return false;
+    ck(lonnx::conv2d(g->ctx, (const float *)x.dptr(), (const float *)w.dptr(), whi, wlo,
+                     has_bias ? (const float *)bias.dptr() : nullptr, res ? (const float *)res->dptr() : nullptr,
+                     (float *)y.dptr_mut(), N, C, H, W, M, kh, kw, (int)strides[0], (int)strides[1], pt, pl, pb, pr,
+                     (int)dil[0], (int)dil[1], group, relu));
     g->env[out_name ? *out_name : n.out.at(0)] = y;
+    return true;
 }
 
 void exec_maxpool(lonnx_graph *g, const NodeDef &n) {
@@ -797,7 +804,7 @@ void exec_node(lonnx_graph *g, const NodeDef &n) {
     if (op == "Sqrt") return exec_unary(g, n, LONNX_SQRT);
     if (op == "Erf") return exec_unary(g, n, LONNX_ERF);
     if (op == "MatMul") return exec_matmul(g, n);
-    if (op == "Conv") return exec_conv(g, n);
+    if (op == "Conv") { exec_conv(g, n); return; }
     if (op == "MaxPool") return exec_maxpool(g, n);
     if (op == "ReduceMean" || op == "ReduceSum" || op == "ReduceMax") return exec_reduce(g, n);
     if (op == "Softmax") return exec_softmax(g, n);
@@ -1138,17 +1145,47 @@ bool match_attn(Matcher &m, int i, Step &st, std::vector<int> &heads_nodes) {
     return true;
 }
 
-// Conv -> Relu (Conv output used only by the Relu)
-bool match_conv_relu(Matcher &m, int i, Step &st) {
+// Conv [-> Add(residual)] [-> Relu]: each intermediate used only by the next node
+bool match_conv(Matcher &m, int i, Step &st) {
     const NodeDef &c = m.N(i);
     if (c.op != "Conv") return false;
-    int r = m.only_consumer(c.out[0]);
-    if (!m.free(r) || m.N(r).op != "Relu") return false;
     st = Step();
-    st.kind = S_CONV_RELU;
-    st.nodes = {i, r};
-    st.y = m.N(r).out[0];
+    st.kind = S_CONV;
+    st.nodes = {i};
+    st.y = c.out[0];
+    int nx = m.only_consumer(c.out[0]);
+    if (m.free(nx) && m.N(nx).op == "Add" && m.N(nx).in.size() == 2 && m.N(nx).in[0] != m.N(nx).in[1]) {
+        const NodeDef &A = m.N(nx);
+        st.b = A.in[0] == c.out[0] ? A.in[1] : A.in[0];
+        st.nodes.push_back(nx);
+        st.y = A.out[0];
+        nx = m.only_consumer(A.out[0]);
+    }
+    if (m.free(nx) && m.N(nx).op == "Relu") {
+        st.epi = 1;
+        st.nodes.push_back(nx);
+        st.y = m.N(nx).out[0];
+    }
+    if (st.nodes.size() == 1 && !m.is_init(c.in.size() > 1 ? c.in[1] : std::string())) return false;
     return true;
+}
+
+// Fused Conv step; false (nothing run) when the residual's shape differs
+// from the Conv output, so the nodes run one by one instead.
+bool exec_conv_step(lonnx_graph *g, const Step &s) {
+    const NodeDef &c = g->nodes[s.nodes[0]];
+    Value res;
+    if (!s.b.empty()) {
+        res = lookup(g, s.b);
+        if (res.dtype != DT_FLOAT) return false;
+        Value x = lookup(g, c.in.at(0)), w = lookup(g, c.in.at(1));
+        if (res.shape.size() != 4 || x.shape.size() != 4 || w.shape.size() != 4 || res.shape[0] != x.shape[0] ||
+            res.shape[1] != w.shape[0])
+            return false;  // exec_conv checks the full shape once it knows Ho, Wo
+        ensure_dev(g, res);
+    }
+    const float *whi = s.wt ? (const float *)s.wt->p : nullptr, *wlo = s.wlo ? (const float *)s.wlo->p : nullptr;
+    return exec_conv(g, c, s.epi, &s.y, s.b.empty() ? nullptr : &res, whi, wlo);
 }
 
 void build_steps(lonnx_graph *g, bool fuse) {
@@ -1192,7 +1229,7 @@ void build_steps(lonnx_graph *g, bool fuse) {
     for (int i = 0; i < n; ++i) {
         if (m.used[i]) continue;
         Step st;
-        if (match_conv_relu(m, i, st)) { claim(st); continue; }
+        if (match_conv(m, i, st)) { claim(st); continue; }
     }
     // weight re-layout for GEMM groups: W [K, N] -> [N, K]
     for (auto &st : groups) {
@@ -1203,6 +1240,18 @@ void build_steps(lonnx_graph *g, bool fuse) {
         ck(split_tf32_nk(g->ctx, (const float *)W.dptr(), (float *)st.wt->p, (float *)st.wlo->p, st.K, st.N, 0));
         const Value &B = g->inits.at(st.b);
         st.bias = B.buf;
+    }
+    // conv weights [M, C, kh, kw] = [M, K] -> tf32 hi / lo [M, ldk] once
+    for (auto &st : groups) {
+        if (st.kind != S_CONV) continue;
+        const NodeDef &c = g->nodes[st.nodes[0]];
+        if (c.in.size() < 2 || !g->inits.count(c.in[1])) continue;
+        const Value &W = g->inits.at(c.in[1]);
+        if (W.dtype != DT_FLOAT || W.shape.size() != 4) continue;
+        const int M = (int)W.shape[0], K = (int)(W.shape[1] * W.shape[2] * W.shape[3]), ldk = (K + 3) & ~3;
+        st.wt = std::make_shared<DevBuf>(g->ctx, (size_t)M * ldk * 4);
+        st.wlo = std::make_shared<DevBuf>(g->ctx, (size_t)M * ldk * 4);
+        ck(split_pad_rows(g->ctx, (const float *)W.dptr(), (float *)st.wt->p, (float *)st.wlo->p, M, K, ldk));
     }
     // QKV merge: three GEMM groups on one input feeding one attention group
     for (auto &at : groups) {
@@ -1274,7 +1323,7 @@ void run_steps(lonnx_graph *g) {
         case S_GEMM: done = exec_gemm_step(g, s); break;
         case S_LN: done = exec_ln_step(g, s); break;
         case S_ATTN: done = exec_attn_step(g, s); break;
-        case S_CONV_RELU: exec_conv(g, g->nodes[s.nodes[0]], 1, &s.y); done = true; break;
+        case S_CONV: done = exec_conv_step(g, s); break;
         default: break;
         }
         if (!done) {

@@ -87,6 +87,27 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
 // hi = w with the low 13 mantissa bits cleared, lo = w - hi (exact).
 int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans);
 int64_t gemm_tc_min_work();
+// Implicit-GEMM convolution geometry for the tensor-core kernel: x == nullptr
+// selects the plain GEMM (A by TMA).  img_rows > 0 writes C as NCHW
+// (row = image * img_rows + pixel, column = channel); res (same layout as
+// C) is added after the bias and before the activation.
+struct ConvArgs {
+    const float *x = nullptr;
+    int C = 0, H = 0, W = 0, kh = 0, kw = 0, sh = 1, sw = 1, pt = 0, pl = 0, dh = 1, dw = 1, Ho = 0, Wo = 0;
+    int img_rows = 0;
+    const float *res = nullptr;
+};
+// y[N, M, Ho, Wo] = conv(x, W) + bias (+ res) (ReLU if epi); W pre-split
+// into Whi, Wlo [M, ldw] (K = C*kh*kw columns used).  P = N*Ho*Wo.
+int conv_tc(lonnx_ctx *ctx, const ConvArgs &cv, const float *Whi, const float *Wlo, int ldw, const float *bias,
+            float *y, int P, int M, int K, int epi);
+// weight [M, K] -> hi, lo [M, ldk] (tf32 split, zero padded)
+int split_pad_rows(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int M, int K, int ldk);
+// Conv with optional pre-split weights (whi/wlo [M, ldk], ldk = (K+3)&~3, or
+// nullptr) and an optional residual added before the ReLU.
+int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, const float *wlo, const float *bias,
+           const float *res, float *y, int N, int C, int H, int W, int M, int kh, int kw, int sh, int sw, int pt,
+           int pl, int pb, int pr, int dh, int dw, int group, int relu);
 // Fused attention on tensor cores (dh = 32, S <= 128); LONNX_E_UNSUPPORTED otherwise.
 int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld, const float *mask,
                  float *out, int B, int S, int heads, int dh, float scale);

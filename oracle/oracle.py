@@ -401,7 +401,9 @@ def run_node(node, get, opset=13, honor_conv_attrs=False):
         return [matmul(I(0), I(1))]
     if op == "Conv":
         if honor_conv_attrs:
-            return [conv(I(0), I(1), I(2), a.get("auto_pad"), a.get("dilations"), a.get("group"),
+            # ONNX: an absent auto_pad is NOTSET, i.e. the explicit pads apply
+            ap = a.get("auto_pad") or ("NOTSET" if a.get("pads") is not None else None)
+            return [conv(I(0), I(1), I(2), ap, a.get("dilations"), a.get("group"),
                          a.get("kernel_shape"), a.get("pads"), a.get("strides"))]
         return [conv(I(0), I(1), I(2), a.get("auto_pad"))]
     if op == "MaxPool":

@@ -117,3 +117,25 @@ def test_cuda_graph_replay_matches_execute(ctx, which):
         cg.replay()
     for o in g.outputs:
         assert np.array_equal(cg.output(o), ref[o])
+
+
+@pytest.mark.parametrize("res_shape", ["same", "broadcast"])
+def test_conv_add_relu_fusion_vs_oracle(ctx, res_shape):
+    """Conv -> Add(residual) -> Relu runs as one tensor-core conv with the
+    residual in the epilogue; a broadcast Add operand cannot fuse and the
+    nodes run one by one -- both against the oracle."""
+    from onnx_b200.graph import ComputationalGraph
+    from onnx_b200.graphs import GraphDef, Node
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((128, 64, 3, 3)) / 24).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, 128).astype(np.float32)
+    rshape = (2, 128, 20, 20) if res_shape == "same" else (1, 128, 1, 1)
+    nodes = [Node("Conv", ["x", "w", "b"], ["c"], {"pads": [1, 1, 1, 1]}),
+             Node("Add", ["r", "c"], ["s"]),
+             Node("Relu", ["s"], ["y"])]
+    g = GraphDef(nodes, {"w": w, "b": b}, ["x", "r"], ["y"])
+    feeds = {"x": rng.uniform(-1, 1, (2, 64, 20, 20)).astype(np.float32),
+             "r": rng.uniform(-1, 1, rshape).astype(np.float32)}
+    got = ComputationalGraph(g, ctx, honor_conv_attrs=True).execute(feeds)["y"]
+    ref = O.execute(g, feeds, honor_conv_attrs=True)["y"]
+    close(got, ref)

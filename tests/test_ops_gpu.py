@@ -274,10 +274,14 @@ def test_attention_direct(ctx):
 @pytest.mark.parametrize("xs,ws,stride,pad,relu", [((4, 64, 28, 28), (128, 64, 3, 3), 1, 1, 1),
                                                    ((2, 3, 64, 64), (64, 3, 7, 7), 2, 3, 1),
                                                    ((4, 256, 14, 14), (512, 256, 1, 1), 2, 0, 0),
-                                                   ((3, 32, 17, 19), (48, 32, 3, 3), 1, 1, 0)])
+                                                   ((3, 32, 17, 19), (48, 32, 3, 3), 1, 1, 0),
+                                                   ((8, 512, 7, 7), (2048, 512, 1, 1), 1, 0, 1),
+                                                   ((5, 128, 9, 13), (72, 128, 3, 3), 2, 2, 0),
+                                                   ((2, 6, 40, 40), (200, 6, 5, 5), 1, 2, 1)])
 def test_conv_tensor_core_path_vs_oracle(ctx, xs, ws, stride, pad, relu):
-    """Convs large enough for the tensor-core GEMM formulation (im2col rows,
-    3xTF32, per-channel bias + ReLU epilogue, NHWC -> NCHW)."""
+    """Convs large enough for the tensor-core implicit GEMM (rows = output
+    pixels gathered from NCHW in the kernel, 3xTF32, bias + ReLU epilogue,
+    NCHW written directly; 7x7 maps put several images in one row tile)."""
     from onnx_b200 import _native as N
     from onnx_b200.tensor import DeviceTensor
     rng = np.random.default_rng(xs[1] + ws[0])
@@ -293,3 +297,30 @@ def test_conv_tensor_core_path_vs_oracle(ctx, xs, ws, stride, pad, relu):
                                    ws[2], ws[3], stride, stride, pad, pad, pad, pad, 1, 1, 1, relu))
     ctx.sync()
     close(y.to_host(), ref)
+
+
+@pytest.mark.parametrize("dil,pads", [((2, 2), (2, 2, 2, 2)), ((1, 3), (1, 0, 2, 3))])
+def test_conv_tensor_core_dilation_asymmetric_pads(ctx, dil, pads):
+    """Dilated taps and asymmetric pads through the implicit-GEMM gather,
+    against a float64 direct convolution (tolerance of the 3xTF32 GEMM)."""
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    rng = np.random.default_rng(11)
+    n, c, h, w, m, k = 3, 40, 23, 21, 96, 3
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((m, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32)
+    pt, pl, pb, pr = pads
+    ho = (h + pt + pb - (dil[0] * (k - 1) + 1)) + 1
+    wo = (w + pl + pr - (dil[1] * (k - 1) + 1)) + 1
+    xp = np.pad(x.astype(np.float64), ((0, 0), (0, 0), (pt, pb), (pl, pr)))
+    ref = np.zeros((n, m, ho, wo))
+    for ky in range(k):
+        for kx in range(k):
+            patch = xp[:, :, ky * dil[0]:ky * dil[0] + ho, kx * dil[1]:kx * dil[1] + wo]
+            ref += np.einsum("nchw,mc->nmhw", patch, wt[:, :, ky, kx].astype(np.float64))
+    dx, dw = DeviceTensor.from_host(ctx, x), DeviceTensor.from_host(ctx, wt)
+    y = DeviceTensor(ctx, (n, m, ho, wo), np.float32)
+    N.check(N.lib.lonnx_conv2d_f32(ctx.handle, dx.ptr, dw.ptr, None, y.ptr, n, c, h, w, m, k, k, 1, 1, pt, pl, pb, pr,
+                                   dil[0], dil[1], 1, 0))
+    ctx.sync()
+    close(y.to_host(), ref.astype(np.float32), atol=1e-5, rtol=1e-5)
