@@ -259,6 +259,37 @@ def resnet_throughput(ctx, st, torch, batch=64, reps=5):
             "tflops_algorithmic": round(fl * batch / (ms * 1e-3) / 1e12, 2)}
 
 
+def conv_case(ctx, st, torch, spec, reps=5):
+    """One Conv (N,C,H,M,k,stride; pad k//2, bias, ReLU) through the C-ABI,
+    CUDA-event timed; for profiler captures of the implicit-GEMM conv."""
+    from onnx_b200 import _native as N_
+    from onnx_b200.tensor import DeviceTensor
+    n, c, h, m, k, s = spec
+    rng = np.random.default_rng(0)
+    x = DeviceTensor.from_host(ctx, rng.uniform(0, 1, (n, c, h, h)).astype(np.float32))
+    w = DeviceTensor.from_host(ctx, (rng.standard_normal((m, c, k, k)) * 0.05).astype(np.float32))
+    b = DeviceTensor.from_host(ctx, rng.uniform(-0.1, 0.1, m).astype(np.float32))
+    p = k // 2
+    ho = (h + 2 * p - k) // s + 1
+    y = DeviceTensor(ctx, (n, m, ho, ho), np.float32)
+
+    def run():
+        N_.check(N_.lib.lonnx_conv2d_f32(ctx.handle, x.ptr, w.ptr, b.ptr, y.ptr, n, c, h, h, m, k, k, s, s, p, p, p, p,
+                                         1, 1, 1, 1))
+    for _ in range(3):
+        run()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        run()
+    e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    fl = 2.0 * n * ho * ho * m * c * k * k
+    return {"conv": list(spec), "us": round(ms * 1e3, 1), "tflops_algorithmic": round(fl / (ms * 1e-3) / 1e12, 1)}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -271,6 +302,8 @@ def main():
     ap.add_argument("--no-resnet", action="store_true")
     ap.add_argument("--resnet-case", type=int, default=0, metavar="B",
                     help="run only the ResNet-50 forward at batch B and exit (for profiler captures)")
+    ap.add_argument("--conv-case", default="", metavar="N,C,H,M,k,s",
+                    help="time one Conv through the C-ABI and exit (for profiler captures)")
     ap.add_argument("--roofline-case", action="store_true",
                     help="run only the roofline GEMM (FFN1 shape) and exit (for ncu captures)")
     ap.add_argument("--profile-case", type=int, default=0, metavar="B",
@@ -278,6 +311,13 @@ def main():
     args = ap.parse_args()
     if args.profile_case:
         return profile_case(args.profile_case)
+    if args.conv_case:
+        import torch
+        from onnx_b200.tensor import Context
+        ctx = Context(0)
+        spec = [int(v) for v in args.conv_case.split(",")]
+        print(json.dumps(conv_case(ctx, torch.cuda.ExternalStream(ctx.stream), torch, spec)))
+        return
     if args.resnet_case:
         import torch
         from onnx_b200.tensor import Context

@@ -44,19 +44,38 @@ constexpr int A_TILE = BM * BK * 4;     // 16 KB
 constexpr int kThreads = 640;           // 20 warps
 // warp roles: 0 TMA, 1 MMA + TMEM owner, 4-7 A -> TMEM, 8-19 accumulate/epilogue
 constexpr int W_TMA = 0, W_MMA = 1, W_A0 = 4, W_ACC0 = 8;
+// kernel modes: plain GEMM (A by TMA, row-major C, one tile per CTA);
+// implicit conv (A gathered, NCHW C, persistent); implicit conv + residual
+constexpr int MODE_GEMM = 0, MODE_CONV = 1, MODE_CONV_RES = 2;
 
-template <int BN>
+// RES: the conv epilogue adds a residual tile, prefetched into shared memory
+// (BM x BN fp32) while the tile's mainloop runs; it costs one ring stage.
+template <int BN, bool RES = false>
 struct Cfg {
     static constexpr int W_TILE = BN * BK * 4;
-    static constexpr int STAGE = A_TILE + 2 * W_TILE;  // TMA ring: A, W_hi, W_lo
-    static constexpr int STAGES = (4 * STAGE + 1280 <= 227 * 1024) ? 4 : 3;
-    static constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int STAGE = A_TILE + 2 * W_TILE;  // ring slot: A, W_hi, W_lo
+    static constexpr int SMEM = 227 * 1024;
+    static constexpr int RES_BYTES = RES ? BM * BN * 4 : 0;
+    static constexpr int FIT = (SMEM - 1024 - 256 - 2 * BN * 4 - RES_BYTES - (RES ? 4096 : 0)) / STAGE;
+    static constexpr int STAGES = FIT > 6 ? 6 : FIT;
+    static_assert(STAGES >= 2, "ring too shallow");
+    static constexpr int RES_OFF = STAGES * STAGE + 256 + 2 * BN * 4;  // after ring, barriers, bias
+    static constexpr int TAB_OFF = RES_OFF + RES_BYTES;  // the rest holds the conv tap table
+    static constexpr int TAB_MAX = (SMEM - 1024 - TAB_OFF) / 4;  // tap-table entries
     static constexpr int GROUPS = BN / 64;              // accumulator column groups of 64
+    static constexpr int NACC = 4 * GROUPS;             // accumulator warps 8 .. 8 + NACC - 1
+    // A warpgroups: warps 4-7, plus warps 8 + NACC .. +3 when the
+    // accumulators leave four warps idle (BN <= 128); each group then moves
+    // 16 of a stage's 32 K-columns
+    static constexpr int NAG = (20 - W_ACC0 - NACC) >= 4 ? 2 : 1;
+    static constexpr int W_A1 = W_ACC0 + NACC;
     static constexpr int ACC_COL = 0;                   // TMEM: 2 chunk accumulators [0, 2 BN)
     static constexpr int A_COL = 2 * BN;                // then NAB A buffers of 64 (hi 32 | lo 32)
     static constexpr int NAB = 2 * BN + 3 * 64 <= 512 ? 3 : 2;
     static constexpr int TMEM_COLS = 2 * BN + NAB * 64 <= 256 ? 256 : 512;
+    static_assert(3 * STAGES + 5 + NAB <= 30, "barrier area");
 };
+
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
@@ -78,27 +97,47 @@ __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__flo
 // core's accumulator rounds toward zero, so one TMEM accumulator over all of
 // K builds an error that grows linearly with K (measured ~10x the
 // sequential fp32 sum at K = 1536); 32-wide chunks keep it at fp32 level.
-template <int BN>
+//
+// Tiles: tile t = (t / ntn) row block, (t % ntn) column block; CTA b takes
+// tiles b, b + gridDim.x, ...  Every role walks one global sequence of
+// (tile, stage) steps, so ring slots and barrier phases carry across tiles
+// and the accumulator warps' epilogue of one tile overlaps the next tile's
+// loads and MMAs.  The row-major epilogue stages C through the ring, so it
+// needs one tile per CTA (grid = tiles); the NCHW epilogue (conv) stores from
+// registers and runs persistent (grid = SMs).
+//
+// Implicit-GEMM conv (cv.x != nullptr): no A tensor map; row r of a tile is
+// output pixel m0 + r, column k is (c, ky, kx), and the A warps gather the
+// taps from the NCHW input themselves (cp.async into the ring's A slots).
+template <int BN, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
               const __grid_constant__ CUtensorMap tmWlo, const float *__restrict__ bias, float *__restrict__ C,
               int M, int N, int K, int ldc, float alpha, float beta, int epi, int *dev_flags,
               const lonnx::ConvArgs cv) {
-    using G = Cfg<BN>;
+    constexpr bool CONV = MODE != MODE_GEMM, RES = MODE == MODE_CONV_RES;
+    using G = Cfg<BN, RES>;
     constexpr int S = G::STAGES;
-    constexpr int NACC = 4 * G::GROUPS;  // accumulator warps in use
+    constexpr int NACC = G::NACC, NAG = G::NAG, NAB = G::NAB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * G::STAGE);
     // [0,S) full  [S,2S) A in TMEM  [2S,3S) stage free  [3S,3S+2) chunk ready
     // [3S+2,3S+4) chunk drained  [3S+4] abort drain  [3S+5,3S+5+NAB) TMEM A buffer free
-    constexpr int NAB = G::NAB;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 5 + NAB);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *ebias = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 256);  // [2][BN], NCHW epilogue
+    uint32_t *tab = reinterpret_cast<uint32_t *>(smem + G::TAB_OFF);                      // conv tap table
+    float *sres = reinterpret_cast<float *>(smem + G::RES_OFF);  // [BN][BM] residual tile (RES)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int nk = (K + BK - 1) / BK;
+    const int ntn = (N + BN - 1) / BN, ntiles = ntn * ((M + BM - 1) / BM);
+    const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int total = my_tiles * nk;  // (tile, stage) steps of this CTA
+    auto tile_n0 = [&](int t) { return (t % ntn) * BN; };
+    auto tile_m0 = [&](int t) { return (t / ntn) * BM; };
+    auto step_tile = [&](int j) { return (int)blockIdx.x + (j / nk) * (int)gridDim.x; };
 
     auto full = [&](int s) { return smem_u32(bars + s); };
     auto conv = [&](int s) { return smem_u32(bars + S + s); };
@@ -115,7 +154,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full(s), 1);
-            mbar_init(conv(s), 4);  // one arrive per A warp
+            mbar_init(conv(s), 4 * NAG);  // one arrive per A warp
             mbar_init(empty(s), 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -126,9 +165,23 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         mbar_init(drainbar, 1);
         *abort_flag = 0;
         fence_mbar_init();
-        prefetch_tmap(&tmA);
+        if constexpr (!CONV) prefetch_tmap(&tmA);
         prefetch_tmap(&tmW);
         prefetch_tmap(&tmWlo);
+    }
+    if (CONV && cv.tab) {
+        // tap table: entry k = (plane offset of tap k) << 8 | (ky * kw + kx);
+        // entries past K (to the next stage) get tap index 63, a bit no
+        // pixel's validity mask has, so they read as zero
+        const int khw = cv.kh * cv.kw, kend = (K + BK - 1) / BK * BK;
+        for (int k = threadIdx.x; k < kend; k += kThreads) {
+            uint32_t e = 63u;
+            if (k < K) {
+                const int c = k / khw, rr = k - c * khw, ky = rr / cv.kw, kx = rr - ky * cv.kw;
+                e = ((uint32_t)(c * cv.H * cv.W + ky * cv.dh * cv.W + kx * cv.dw) << 8) | (uint32_t)rr;
+            }
+            tab[k] = e;
+        }
     }
     if (warp == W_MMA) {
         tmem_alloc(smem_u32(tmem_slot), G::TMEM_COLS);
@@ -139,32 +192,45 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     bool ok = true;
+    const int agroup = (warp >= W_A0 && warp < W_A0 + 4) ? 0 : (NAG == 2 && warp >= G::W_A1 && warp < G::W_A1 + 4) ? 1 : -1;
 
     if (warp == W_TMA) {
         if (lane == 0) {
-            const uint32_t bytes = cv.x ? 2 * G::W_TILE : G::STAGE;
-            for (int i = 0; i < nk && ok; ++i) {
-                const int s = i % S;
-                if (!mbar_wait(empty(s), ((i / S) & 1) ^ 1, abort_flag)) { ok = false; break; }
+            constexpr uint32_t bytes = CONV ? 2 * G::W_TILE : G::STAGE;
+            // (tile, K offset) advanced incrementally: no divisions on the issue path
+            int t = (int)blockIdx.x, k0 = 0, s = 0, ph = 0;
+            int n0 = tile_n0(t), m0 = tile_m0(t);
+            for (int j = 0; j < total && ok; ++j) {
+                if (!mbar_wait(empty(s), ph ^ 1, abort_flag)) { ok = false; break; }
                 mbar_arrive_expect_tx(full(s), bytes);
-                if (!cv.x) tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), i * BK, m0);
-                tma_load_2d(smem_u32(stageW(s)), &tmW, full(s), i * BK, n0);
-                tma_load_2d(smem_u32(stageWlo(s)), &tmWlo, full(s), i * BK, n0);
-                issued = i + 1;
+                if constexpr (!CONV) tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), k0, m0);
+                tma_load_2d(smem_u32(stageW(s)), &tmW, full(s), k0, n0);
+                tma_load_2d(smem_u32(stageWlo(s)), &tmWlo, full(s), k0, n0);
+                issued = j + 1;
+                if (++s == S) { s = 0; ph ^= 1; }
+                k0 += BK;
+                if (k0 >= nk * BK) {
+                    k0 = 0;
+                    t += (int)gridDim.x;
+                    n0 = tile_n0(t);
+                    m0 = tile_m0(t);
+                }
             }
         }
     } else if (warp == W_MMA) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(BM, BN);
-            for (int i = 0; i < nk && ok; ++i) {
-                const int s = i % S, b = i & 1;
-                if (!mbar_wait(conv(s), (i / S) & 1, abort_flag)) { ok = false; break; }
+            for (int j = 0; j < total && ok; ++j) {
+                const int s = j % S, b = j & 1;
+                if (!mbar_wait(conv(s), (j / S) & 1, abort_flag)) { ok = false; break; }
                 // implicit conv: the A warps do not wait for the W tiles, so the MMA does
-                if (cv.x && !mbar_wait(full(s), (i / S) & 1, abort_flag)) { ok = false; break; }
-                if (!mbar_wait(tdrain(b), ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                if constexpr (CONV) {
+                    if (!mbar_wait(full(s), (j / S) & 1, abort_flag)) { ok = false; break; }
+                }
+                if (!mbar_wait(tdrain(b), ((j >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t acc = tmem + G::ACC_COL + b * BN;
-                const int ab = i % NAB;
+                const int ab = j % NAB;
                 const uint32_t ahi = tmem + G::A_COL + ab * 64, alo = ahi + 32;
                 const uint32_t w = smem_u32(stageW(s)), wlo = smem_u32(stageWlo(s));
 #pragma unroll
@@ -179,35 +245,98 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 mma_commit(tfull(b));
             }
         }
-    } else if (warp >= W_A0 && warp < W_A0 + 4) {
+    } else if (agroup >= 0) {
         // A warps: warp (w % 4) owns TMEM lanes = tile rows 32*(w%4)..+31;
-        // each thread moves its row of the stage's A tile into TMEM as
-        // hi = tf32(a) and lo = a - hi
-        const int q = warp & 3, r = q * 32 + lane;
+        // each thread moves its row's K-columns [c0, c0 + NC) of every stage
+        // into TMEM as hi = tf32(a) and lo = a - hi
+        constexpr int NC = BK / NAG;
+        const int q = warp & 3, r = q * 32 + lane, c0 = agroup * NC;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::A_COL;
-        if (cv.x) {
-            // implicit-GEMM conv: row r is output pixel m0 + r, column k is
-            // (c, ky, kx).  Each thread gathers its pixel's 32 taps of a
-            // stage straight from the NCHW input with 4-byte cp.async into
-            // its own row of the stage's (otherwise unused) A slot, S - 1
-            // stages ahead; lanes are consecutive pixels, so each tap is one
-            // coalesced warp access; taps outside the image or past K are
-            // zero-filled.  Rows are rotated by r words so the 32 lanes hit
-            // 32 banks.
-            constexpr int D = S - 1;
-            int iy0 = -(1 << 20), ix0 = 0;
-            const float *xr = cv.x;
-            const int p = m0 + r;
-            if (p < M) {
-                const int hw = cv.Ho * cv.Wo, n = p / hw, rem = p - n * hw;
-                const int oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
-                iy0 = oy * cv.sh - cv.pt;
-                ix0 = ox * cv.sw - cv.pl;
-                xr = cv.x + (int64_t)n * cv.C * cv.H * cv.W + (int64_t)iy0 * cv.W + ix0;
+        auto to_tmem = [&](int b, const float *x) {
+#pragma unroll
+            for (int h = 0; h < NC / 16; ++h) {
+                uint32_t hi[16], lo[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const float v = x[h * 16 + u], hv = tf32_hi(v);
+                    hi[u] = __float_as_uint(hv);
+                    lo[u] = __float_as_uint(__fsub_rn(v, hv));
+                }
+                tmem_st_32x32b_x16(lane_base + b * 64 + c0 + h * 16, hi);
+                tmem_st_32x32b_x16(lane_base + b * 64 + 32 + c0 + h * 16, lo);
             }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+        };
+        if constexpr (CONV) {
+            // implicit-GEMM conv: each thread gathers its pixel's taps of a
+            // stage straight from the NCHW input with 4-byte cp.async into
+            // its own row of the ring's A slot, S - 1 steps ahead; lanes are
+            // consecutive pixels, so each tap is one coalesced warp access;
+            // taps outside the image or past K are zero-filled.  Rows are
+            // rotated by r words so the 32 lanes hit 32 banks.
+            constexpr int D = S - 1;
+            int cur_tile = -1, iy0 = 0, ix0 = 0;
+            const float *xr = cv.x;
             const int khw = cv.kh * cv.kw, HW = cv.H * cv.W;
-            auto gather = [&](int i) {
-                const uint32_t row = smem_u32(stageA(i % S)) + r * 128;
+            // table path: incremental (tile, stage) of the next gather, the
+            // pixel's validity mask over the kh x kw taps for the current tile
+            int gt = (int)blockIdx.x, gi = 0, gj = 0, mt = -1;
+            uint64_t vmask = 0;
+            auto gather_tab = [&]() {
+                if (gt != mt) {
+                    mt = gt;
+                    const int p = tile_m0(gt) + r;
+                    vmask = 0;
+                    xr = cv.x;
+                    if (p < M) {
+                        const int hw = cv.Ho * cv.Wo, n = p / hw, rem = p - n * hw;
+                        const int oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
+                        const int y0 = oy * cv.sh - cv.pt, x0 = ox * cv.sw - cv.pl;
+                        xr = cv.x + (int64_t)n * cv.C * HW + (int64_t)y0 * cv.W + x0;
+                        int ky = 0, kx = 0;
+                        for (int rr = 0; rr < khw; ++rr) {
+                            const int yy = y0 + ky * cv.dh, xx = x0 + kx * cv.dw;
+                            if ((unsigned)yy < (unsigned)cv.H && (unsigned)xx < (unsigned)cv.W) vmask |= 1ull << rr;
+                            if (++kx == cv.kw) { kx = 0; ++ky; }
+                        }
+                    }
+                }
+                const uint32_t row = smem_u32(stageA(gj % S)) + r * 128;
+                const uint4 *te = reinterpret_cast<const uint4 *>(tab + gi * BK + c0);
+#pragma unroll
+                for (int u4 = 0; u4 < NC / 4; ++u4) {
+                    const uint4 e4 = te[u4];  // 4 taps, same address in every lane
+                    const uint32_t e[4] = {e4.x, e4.y, e4.z, e4.w};
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) {
+                        const int u = c0 + u4 * 4 + v;
+                        const bool in = (vmask >> (e[v] & 255u)) & 1u;
+                        cp_async4(row + (((u + r) & 31) << 2), in ? xr + (e[v] >> 8) : cv.x, in ? 4u : 0u);
+                    }
+                }
+                ++gj;
+                if (++gi == nk) { gi = 0; gt += (int)gridDim.x; }
+            };
+            auto gather = [&](int j) {
+                if (cv.tab) { gather_tab(); return; }
+                const int t = step_tile(j), i = j % nk;
+                if (t != cur_tile) {
+                    cur_tile = t;
+                    const int p = tile_m0(t) + r;
+                    iy0 = -(1 << 20);
+                    ix0 = 0;
+                    xr = cv.x;
+                    if (p < M) {
+                        const int hw = cv.Ho * cv.Wo, n = p / hw, rem = p - n * hw;
+                        const int oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
+                        iy0 = oy * cv.sh - cv.pt;
+                        ix0 = ox * cv.sw - cv.pl;
+                        xr = cv.x + (int64_t)n * cv.C * HW + (int64_t)iy0 * cv.W + ix0;
+                    }
+                }
+                const uint32_t row = smem_u32(stageA(j % S)) + r * 128;
                 const int k = i * BK + lane;
                 int off = 0, dy = -(1 << 20), dx = 0;  // taps past K read as zero
                 if (k < K) {
@@ -216,8 +345,8 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                     dx = kx * cv.dw;
                     off = c * HW + dy * cv.W + dx;
                 }
-#pragma unroll 4
-                for (int u = 0; u < BK; ++u) {
+#pragma unroll
+                for (int u = c0; u < c0 + NC; ++u) {
                     const int o = __shfl_sync(0xffffffffu, off, u);
                     const int yy = iy0 + __shfl_sync(0xffffffffu, dy, u);
                     const int xx = ix0 + __shfl_sync(0xffffffffu, dx, u);
@@ -226,155 +355,174 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 }
             };
             for (int j = 0; j < D; ++j) {
-                if (j < nk) gather(j);
+                if (j < total) gather(j);
                 cp_async_commit();
             }
-            for (int i = 0; i < nk && ok; ++i) {
-                const int s = i % S, b = i % NAB;
-                if (i + D < nk) gather(i + D);
+            for (int j = 0; j < total && ok; ++j) {
+                const int s = j % S, b = j % NAB;
+                if (j + D < total) gather(j + D);
                 cp_async_commit();
-                cp_async_wait<D>();  // this thread's taps of stage i have landed
+                cp_async_wait<D>();  // this thread's taps of step j have landed
                 const float *row = reinterpret_cast<const float *>(stageA(s) + r * 128);
-                if (!mbar_wait(afree(b), ((i / NAB) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                tc_fence_after();
+                float x[NC];
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
+                for (int u = 0; u < NC; ++u) x[u] = row[(c0 + u + r) & 31];
+                if (!mbar_wait(afree(b), ((j / NAB) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                to_tmem(b, x);
+                if (lane == 0) mbar_arrive(conv(s));
+            }
+            cp_async_wait<0>();
+        } else {
+            for (int j = 0; j < total && ok; ++j) {
+                const int s = j % S, b = j % NAB;
+                if (!mbar_wait(full(s), (j / S) & 1, abort_flag)) { ok = false; break; }
+                if (!mbar_wait(afree(b), ((j / NAB) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+                const uint8_t *row = stageA(s) + r * 128;
+#pragma unroll
+                for (int h = 0; h < NC / 16; ++h) {
                     uint32_t hi[16], lo[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float x = row[(hf * 16 + j + r) & 31], h = tf32_hi(x);
-                        hi[j] = __float_as_uint(h);
-                        lo[j] = __float_as_uint(__fsub_rn(x, h));
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const int c = c0 / 4 + h * 4 + c4;  // 16-byte chunk, 128B-swizzled
+                        const float4 v = *reinterpret_cast<const float4 *>(row + (((c ^ (r & 7))) << 4));
+                        const float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const float hv = tf32_hi(x[u]);
+                            hi[c4 * 4 + u] = __float_as_uint(hv);
+                            lo[c4 * 4 + u] = __float_as_uint(__fsub_rn(x[u], hv));
+                        }
                     }
-                    tmem_st_32x32b_x16(lane_base + b * 64 + hf * 16, hi);
-                    tmem_st_32x32b_x16(lane_base + b * 64 + 32 + hf * 16, lo);
+                    tmem_st_32x32b_x16(lane_base + b * 64 + c0 + h * 16, hi);
+                    tmem_st_32x32b_x16(lane_base + b * 64 + 32 + c0 + h * 16, lo);
                 }
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(conv(s));
             }
-            cp_async_wait<0>();
-        }
-        for (int i = 0; i < nk && ok && !cv.x; ++i) {
-            const int s = i % S, b = i % NAB;
-            if (!mbar_wait(full(s), (i / S) & 1, abort_flag)) { ok = false; break; }
-            if (!mbar_wait(afree(b), ((i / NAB) & 1) ^ 1, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            const uint8_t *row = stageA(s) + r * 128;
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                uint32_t hi[16], lo[16];
-#pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-                    const int c = hf * 4 + c4;
-                    const float4 v = *reinterpret_cast<const float4 *>(row + (((c ^ (r & 7))) << 4));
-                    const float x[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float h = tf32_hi(x[u]);
-                        hi[c4 * 4 + u] = __float_as_uint(h);
-                        lo[c4 * 4 + u] = __float_as_uint(__fsub_rn(x[u], h));
-                    }
-                }
-                tmem_st_32x32b_x16(lane_base + b * 64 + hf * 16, hi);
-                tmem_st_32x32b_x16(lane_base + b * 64 + 32 + hf * 16, lo);
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(conv(s));
         }
     } else if (warp >= W_ACC0 && warp < W_ACC0 + NACC) {
         // accumulator / epilogue warps: warp w owns TMEM lanes 32*(w%4)..+31
         // (tile rows) and one 64-column group of the tile
         const int q = warp & 3, grp = (warp - W_ACC0) >> 2;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::ACC_COL + grp * 64;
-        float acc[64];
-#pragma unroll
-        for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
-        for (int i = 0; i < nk && ok; ++i) {
-            const int b = i & 1;
-            if (!mbar_wait(tfull(b), (i >> 1) & 1, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t rr[16];
-                tmem_ld_32x32b_x16(lane_base + b * BN + c * 16, rr);
-                tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 16; ++j) acc[c * 16 + j] = __fadd_rn(acc[c * 16 + j], __uint_as_float(rr[j]));
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tdrain(b));
-        }
-        // epilogue: raw sums staged row-major in the (now idle) stage buffers,
-        // then one pass that applies alpha, bias and the activation and writes
-        // coalesced 16-byte stores.  The activation code appears once (a
-        // per-element unrolled epilogue with Erf-GELU inlined overflows the
-        // instruction cache).
-        constexpr int PITCH = BN + 4;  // floats; keeps the per-row writes conflict-free
-        static_assert(BM * PITCH * 4 + BN * 4 <= G::STAGES * G::STAGE, "C tile + bias must fit in the stage ring");
-        float *ctile = reinterpret_cast<float *>(smem);
-        float *sbias = ctile + BM * PITCH;
-        const int t = threadIdx.x - W_ACC0 * 32;
-        for (int c = t; c < BN; c += NACC * 32) {
-            const int col = n0 + c;
-            float bv = 0.0f;
-            if (bias && col < N) bv = beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col));
-            sbias[c] = bv;
-        }
         const int rloc = q * 32 + lane;
-        if (cv.img_rows > 0) {
-            // NCHW output: row = (image, pixel), column = channel; a warp's
-            // lanes hold consecutive pixels, so each column store coalesces.
-            // Optional residual (same layout) added after the bias, before
-            // the activation, as a following Add node would.
-            asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
-            const int grow = m0 + rloc;
-            if (ok && grow < M) {
-                const int img = grow / cv.img_rows, pix = grow - img * cv.img_rows;
-                const int64_t o = (int64_t)img * N * cv.img_rows + pix;
-                float *dst = C + o;
-                const float *rs = cv.res ? cv.res + o : nullptr;
-                const int cs = cv.img_rows;  // N * img_rows (one image's output) < 2^31
-#pragma unroll
-                for (int j0 = 0; j0 < 64; j0 += 8) {
-                    // residual loads for 8 columns first (all in flight at once)
-                    float rv[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int col = min(n0 + grp * 64 + j0 + j, N - 1);
-                        rv[j] = rs ? __ldg(rs + col * cs) : 0.0f;
+        for (int tt = 0; tt < my_tiles && ok; ++tt) {
+            const int t = (int)blockIdx.x + tt * (int)gridDim.x, n0 = tile_n0(t), m0 = tile_m0(t);
+            if constexpr (RES) {
+                // this thread's residual row (its pixel, its 64 channels) into
+                // shared memory now; only this thread reads it back, after a
+                // wait on its own copy group, in the epilogue
+                const int grow = m0 + rloc;
+                if (grow < M) {
+                    const int img = grow / cv.img_rows, pix = grow - img * cv.img_rows;
+                    const float *rs = cv.res + (int64_t)img * N * cv.img_rows + pix;
+                    const uint32_t d0 = smem_u32(sres) + (uint32_t)(grp * 64 * BM + rloc) * 4;
+#pragma unroll 8
+                    for (int u = 0; u < 64; ++u) {
+                        const int col = n0 + grp * 64 + u;
+                        cp_async4(d0 + u * BM * 4, col < N ? rs + col * cv.img_rows : cv.res, col < N ? 4u : 0u);
                     }
+                }
+                cp_async_commit();
+            }
+            float acc[64];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int cl = grp * 64 + j0 + j, col = n0 + cl;
-                        if (col < N) {
-                            float x = acc[j0 + j];
-                            if (alpha != 1.0f) x = __fmul_rn(x, alpha);
-                            if (bias) x = __fadd_rn(x, sbias[cl]);
-                            if (rs) x = __fadd_rn(x, rv[j]);
-                            if (epi == LONNX_EPI_RELU) x = x > 0.0f ? x : 0.0f;
-                            dst[col * cs] = x;
+            for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+            for (int i = 0; i < nk && ok; ++i) {
+                const int j = tt * nk + i, b = j & 1;
+                if (!mbar_wait(tfull(b), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t rr[16];
+                    tmem_ld_32x32b_x16(lane_base + b * BN + c * 16, rr);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) acc[c * 16 + u] = __fadd_rn(acc[c * 16 + u], __uint_as_float(rr[u]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tdrain(b));
+            }
+            if (!ok) break;
+            if constexpr (CONV) {
+                // NCHW output: row = (image, pixel), column = channel; a
+                // warp's lanes hold consecutive pixels, so each column store
+                // coalesces.  The optional residual (same layout) is added
+                // after the bias and before the activation, as a following
+                // Add node would.
+                // the tile's bias (times beta) in shared memory, double-buffered
+                // by tile parity: costs no registers in the store loop
+                float *sb = ebias + (tt & 1) * BN;
+                for (int c = threadIdx.x - W_ACC0 * 32; c < BN; c += NACC * 32) {
+                    const int col = n0 + c;
+                    float bv = 0.0f;
+                    if (bias && col < N) bv = beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col));
+                    sb[c] = bv;
+                }
+                asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
+                const int grow = m0 + rloc;
+                if (grow < M) {
+                    const int img = grow / cv.img_rows, pix = grow - img * cv.img_rows;
+                    const int64_t o = (int64_t)img * N * cv.img_rows + pix;
+                    float *dst = C + o;
+                    const int cs = cv.img_rows;  // N * img_rows (one image's output) < 2^31
+                    const int cb = n0 + grp * 64;
+                    const float *sbg = sb + grp * 64;  // zero where there is no bias
+                    const bool relu = epi == LONNX_EPI_RELU;
+                    // x * alpha is exact for alpha == 1, so it is applied unconditionally;
+                    // Relu keeps NaN -> 0 (x > 0 is false for NaN)
+                    if constexpr (!RES) {
+#pragma unroll
+                        for (int u = 0; u < 64; ++u) {
+                            float x = __fadd_rn(__fmul_rn(acc[u], alpha), sbg[u]);
+                            x = (relu && !(x > 0.0f)) ? 0.0f : x;
+                            if (cb + u < N) dst[(cb + u) * cs] = x;
+                        }
+                    } else {
+                        cp_async_wait<0>();
+                        const float *sr = sres + grp * 64 * BM + rloc;
+#pragma unroll
+                        for (int u = 0; u < 64; ++u) {
+                            float x = __fadd_rn(__fmul_rn(acc[u], alpha), sbg[u]);
+                            x = __fadd_rn(x, sr[u * BM]);
+                            x = (relu && !(x > 0.0f)) ? 0.0f : x;
+                            if (cb + u < N) dst[(cb + u) * cs] = x;
                         }
                     }
                 }
+                continue;
             }
-        } else {
-        if (ok) {
+            // row-major epilogue (one tile per CTA, the ring is idle now):
+            // raw sums staged row-major in the stage buffers, then one pass
+            // that applies alpha, bias and the activation and writes
+            // coalesced 16-byte stores.  The activation code appears once (a
+            // per-element unrolled epilogue with Erf-GELU inlined overflows
+            // the instruction cache).
+            constexpr int PITCH = BN + 4;  // floats; keeps the per-row writes conflict-free
+            static_assert(BM * PITCH * 4 + BN * 4 <= G::STAGES * G::STAGE, "C tile + bias must fit in the stage ring");
+            float *ctile = reinterpret_cast<float *>(smem);
+            float *sbias = ctile + BM * PITCH;
+            const int tid = threadIdx.x - W_ACC0 * 32;
+            for (int c = tid; c < BN; c += NACC * 32) {
+                const int col = n0 + c;
+                float bv = 0.0f;
+                if (bias && col < N) bv = beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col));
+                sbias[c] = bv;
+            }
 #pragma unroll
             for (int j = 0; j < 64; j += 4)
                 *reinterpret_cast<float4 *>(ctile + rloc * PITCH + grp * 64 + j) =
                     make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-        }
-        asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
-        if (ok) {
+            asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
             constexpr int V4 = BN / 4;  // float4 per tile row
             const bool vec = (ldc & 3) == 0 && n0 + BN <= N;
 #pragma unroll 1
-            for (int e = t; e < BM * V4; e += NACC * 32) {
+            for (int e = tid; e < BM * V4; e += NACC * 32) {
                 const int rr = e / V4, c4 = e % V4;
                 const int grow = m0 + rr;
                 if (grow >= M) continue;
@@ -398,7 +546,6 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                         if (col0 + u < N) dst[u] = v[u];
                 }
             }
-        }
         }
     }
 
@@ -479,18 +626,24 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
     return LONNX_OK;
 }
 
-template <int BN>
+template <int BN, int MODE>
 int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, const CUtensorMap &mwlo,
               const float *bias, float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi,
               const lonnx::ConvArgs &cv) {
-    using G = Cfg<BN>;
+    using G = Cfg<BN, MODE == MODE_CONV_RES>;
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {
-        LONNX_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, G::SMEM));
+        LONNX_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        G::SMEM));
         attr_set[ctx->device & 63] = true;
     }
-    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-    k_gemm_tf32x3<BN><<<grid, kThreads, G::SMEM, ctx->stream>>>(ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi,
+    const int64_t tiles = (int64_t)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
+    if (tiles >= (1ll << 31)) return lonnx::set_error(LONNX_E_UNSUPPORTED, "gemm_tc: too many tiles");
+    // the NCHW (conv) epilogue needs no shared memory: one persistent CTA per SM
+    const int64_t grid = MODE != MODE_GEMM && tiles > ctx->num_sms ? ctx->num_sms : tiles;
+    // the tap table (the tail of shared memory) exists only for the implicit conv
+    const int smem = MODE != MODE_GEMM ? G::SMEM : G::TAB_OFF + 1024;
+    k_gemm_tf32x3<BN, MODE><<<(unsigned)grid, kThreads, smem, ctx->stream>>>(ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi,
                                                                 ctx->dev_flags, cv);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
@@ -507,6 +660,19 @@ int pick_bn(int N) {
     if (N % 192 == 0) return 192;
     if (N % 128 == 0) return 128;
     return ((N + 191) / 192 * 192 - N) < ((N + 127) / 128 * 128 - N) ? 192 : 128;
+}
+
+// Conv tile width: the least padding of M among 128, 192 and 64 (ties to
+// the wider tile); 64-channel convs get BN = 64 instead of half-empty tiles.
+// With a residual the tile must leave room for it: 128 or 64.
+int pick_bn_conv(int M, bool res) {
+    int best = 128, waste = (M + 127) / 128 * 128 - M;
+    for (int bn : {192, 64}) {
+        if (res && bn == 192) continue;
+        const int w = (M + bn - 1) / bn * bn - M;
+        if (w < waste) { best = bn; waste = w; }
+    }
+    return best;
 }
 
 }  // namespace
@@ -529,8 +695,8 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
     if (rc) return rc;
     (void)allow_scratch;  // this path allocates nothing
     const ConvArgs none{};
-    if (bn == 192) return launch_tc<192>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
-    return launch_tc<128>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
+    if (bn == 192) return launch_tc<192, MODE_GEMM>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
+    return launch_tc<128, MODE_GEMM>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
 }
 
 int conv_tc(lonnx_ctx *ctx, const ConvArgs &cv, const float *Whi, const float *Wlo, int ldw, const float *bias,
@@ -540,15 +706,27 @@ int conv_tc(lonnx_ctx *ctx, const ConvArgs &cv, const float *Whi, const float *W
         (epi != LONNX_EPI_NONE && epi != LONNX_EPI_RELU) || (int64_t)M * cv.img_rows >= (1ll << 31) ||
         (int64_t)cv.C * cv.H * cv.W >= (1ll << 31))
         return set_error(LONNX_E_UNSUPPORTED, "conv_tc: unsupported operands");
-    const int bn = pick_bn(M);
+    const bool res = cv.res != nullptr;
+    const int bn = pick_bn_conv(M, res);
+    ConvArgs a = cv;
+    const int kend = (K + BK - 1) / BK * BK;
+    const int tab_max = bn == 192 ? Cfg<192>::TAB_MAX
+                        : bn == 64 ? (res ? Cfg<64, true>::TAB_MAX : Cfg<64>::TAB_MAX)
+                                   : (res ? Cfg<128, true>::TAB_MAX : Cfg<128>::TAB_MAX);
+    a.tab = kend <= tab_max && cv.kh * cv.kw <= 63 && (int64_t)cv.C * cv.H * cv.W < (1ll << 24);
     CUtensorMap mw, mwlo;
     int rc = make_map(&mw, Whi, M, K, ldw, bn);
     if (rc) return rc;
     rc = make_map(&mwlo, Wlo, M, K, ldw, bn);
     if (rc) return rc;
     // the A map is unused in implicit mode (the kernel gathers A itself)
-    if (bn == 192) return launch_tc<192>(ctx, mw, mw, mwlo, bias, y, P, M, K, 0, 1.0f, 1.0f, epi, cv);
-    return launch_tc<128>(ctx, mw, mw, mwlo, bias, y, P, M, K, 0, 1.0f, 1.0f, epi, cv);
+    if (res) {
+        if (bn == 64) return launch_tc<64, MODE_CONV_RES>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+        return launch_tc<128, MODE_CONV_RES>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+    }
+    if (bn == 192) return launch_tc<192, MODE_CONV>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+    if (bn == 64) return launch_tc<64, MODE_CONV>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+    return launch_tc<128, MODE_CONV>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
 }
 
 int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans) {
@@ -562,3 +740,4 @@ int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, i
 }
 
 }  // namespace lonnx
+

@@ -96,6 +96,7 @@ struct ConvArgs {
     int C = 0, H = 0, W = 0, kh = 0, kw = 0, sh = 1, sw = 1, pt = 0, pl = 0, dh = 1, dw = 1, Ho = 0, Wo = 0;
     int img_rows = 0;
     const float *res = nullptr;
+    int tab = 0;  // set by conv_tc: the per-CTA tap table fits (see gemm_tc.cu)
 };
 // y[N, M, Ho, Wo] = conv(x, W) + bias (+ res) (ReLU if epi); W pre-split
 // into Whi, Wlo [M, ldw] (K = C*kh*kw columns used).  P = N*Ho*Wo.

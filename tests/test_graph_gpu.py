@@ -119,17 +119,19 @@ def test_cuda_graph_replay_matches_execute(ctx, which):
         assert np.array_equal(cg.output(o), ref[o])
 
 
-@pytest.mark.parametrize("res_shape", ["same", "broadcast"])
-def test_conv_add_relu_fusion_vs_oracle(ctx, res_shape):
+@pytest.mark.parametrize("res_shape,m", [("same", 128), ("same", 64), ("same", 320), ("broadcast", 128)])
+def test_conv_add_relu_fusion_vs_oracle(ctx, res_shape, m):
     """Conv -> Add(residual) -> Relu runs as one tensor-core conv with the
-    residual in the epilogue; a broadcast Add operand cannot fuse and the
-    nodes run one by one -- both against the oracle."""
+    residual prefetched into shared memory and added in the epilogue (tile
+    widths 128 and 64, and a ragged last column tile); a broadcast Add
+    operand cannot fuse and the nodes run one by one -- all against the
+    oracle."""
     from onnx_b200.graph import ComputationalGraph
     from onnx_b200.graphs import GraphDef, Node
     rng = np.random.default_rng(3)
-    w = (rng.standard_normal((128, 64, 3, 3)) / 24).astype(np.float32)
-    b = rng.uniform(-0.1, 0.1, 128).astype(np.float32)
-    rshape = (2, 128, 20, 20) if res_shape == "same" else (1, 128, 1, 1)
+    w = (rng.standard_normal((m, 64, 3, 3)) / 24).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, m).astype(np.float32)
+    rshape = (2, m, 20, 20) if res_shape == "same" else (1, m, 1, 1)
     nodes = [Node("Conv", ["x", "w", "b"], ["c"], {"pads": [1, 1, 1, 1]}),
              Node("Add", ["r", "c"], ["s"]),
              Node("Relu", ["s"], ["y"])]

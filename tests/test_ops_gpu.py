@@ -277,11 +277,14 @@ def test_attention_direct(ctx):
                                                    ((3, 32, 17, 19), (48, 32, 3, 3), 1, 1, 0),
                                                    ((8, 512, 7, 7), (2048, 512, 1, 1), 1, 0, 1),
                                                    ((5, 128, 9, 13), (72, 128, 3, 3), 2, 2, 0),
-                                                   ((2, 6, 40, 40), (200, 6, 5, 5), 1, 2, 1)])
+                                                   ((2, 6, 40, 40), (200, 6, 5, 5), 1, 2, 1),
+                                                   ((2, 8, 30, 30), (64, 8, 9, 9), 1, 4, 0)])
 def test_conv_tensor_core_path_vs_oracle(ctx, xs, ws, stride, pad, relu):
     """Convs large enough for the tensor-core implicit GEMM (rows = output
     pixels gathered from NCHW in the kernel, 3xTF32, bias + ReLU epilogue,
-    NCHW written directly; 7x7 maps put several images in one row tile)."""
+    NCHW written directly; 7x7 maps put several images in one row tile; the
+    9x9 kernel has more taps than the tap table takes, so it gathers through
+    the per-stage shuffle path)."""
     from onnx_b200 import _native as N
     from onnx_b200.tensor import DeviceTensor
     rng = np.random.default_rng(xs[1] + ws[0])
