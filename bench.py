@@ -129,6 +129,64 @@ def gemm_roofline(ctx, st, torch, M=32768, K=384, N=1536, reps=20):
             "traffic": _ncu_traffic()}
 
 
+SWEEP = [(128, 384, 384), (4096, 384, 1536), (4096, 1536, 384), (8192, 1024, 4096)]
+
+
+def gemm_sweep(ctx, st, torch, reps=10):
+    """BASELINE's single-op Gemm sweep: Y = A.op(B) + bias through the public
+    C-ABI entry point (lonnx_gemm_f32, alpha = beta = 1, bias [N]), A and B
+    ~ U[-1, 1], transB in {0, 1}.  Each call includes the per-call tf32
+    split of B (the op receives a raw weight).  CUDA events, warm."""
+    from onnx_b200 import _native as Nn
+    from onnx_b200.tensor import DeviceTensor
+    _, bf16, kind = peaks()
+    tf32_peak = bf16 / 2.0
+    rng = np.random.default_rng(7)
+    out = []
+    for M, K, N in SWEEP:
+        A = DeviceTensor.from_host(ctx, rng.uniform(-1, 1, (M, K)).astype(np.float32))
+        bias = DeviceTensor.from_host(ctx, rng.uniform(-1, 1, (N,)).astype(np.float32))
+        C = DeviceTensor(ctx, (M, N), np.float32)
+        for tb in (0, 1):
+            B = DeviceTensor.from_host(ctx, rng.uniform(-1, 1, (N, K) if tb else (K, N)).astype(np.float32))
+            f = lambda: Nn.check(Nn.lib.lonnx_gemm_f32(ctx.handle, A.ptr, B.ptr, bias.ptr, C.ptr, 1, M, N, K, 0, 0, 0,
+                                                       tb, 1.0, 1.0, 0))
+            for _ in range(3):
+                f()
+            ctx.sync()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                f()
+            e1.record(st)
+            e1.synchronize()
+            us = e0.elapsed_time(e1) / reps * 1e3
+            tf = 2.0 * M * N * K / (us * 1e-6) / 1e12
+            out.append({"M": M, "K": K, "N": N, "transB": tb, "us": round(us, 1), "tflops": round(tf, 2),
+                        "frac_tf32": round(tf / tf32_peak, 4), "tensor_pipe_frac": round(3 * tf / tf32_peak, 4)})
+    return {"peak_tf32": tf32_peak, "peak_note": f"dense tf32 = {kind} bf16 / 2; tensor_pipe_frac = 3 x frac_tf32 "
+                                                 "(3xTF32 issues 3 MMAs per product)", "cases": out}
+
+
+def e5_batch(ctx, st, torch, cg, vocab, batch=32, reps=10):
+    """the same encoder at batch 32, device-resident inputs."""
+    from onnx_b200 import graphs as G
+    from onnx_b200.tensor import DeviceTensor
+    inp = {k: DeviceTensor.from_host(ctx, v) for k, v in G.e5_inputs(batch, SEQ, vocab, seed=7).items()}
+    cg.set_inputs(inp)
+    for _ in range(3):
+        cg.run()
+    ctx.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        cg.run()
+    e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    return {"batch": batch, "seq_per_s": round(batch / (ms * 1e-3), 1), "ms_per_batch": round(ms, 3)}
+
+
 def _oracle_graph():
     from onnx_b200 import graphs as G
     g = G.e5_encoder(vocab=250037, seq=SEQ, seed=0)
@@ -399,6 +457,8 @@ def main():
     d2h = out.nbytes
 
     roof = gemm_roofline(ctx, st, torch) if rank == 0 else None
+    sweep = gemm_sweep(ctx, st, torch) if rank == 0 else None
+    b32 = e5_batch(ctx, st, torch, cg, args.vocab) if rank == 0 else None
     mnist = mnist_latency(ctx, st, torch) if rank == 0 else None
     resnet = resnet_throughput(ctx, st, torch) if rank == 0 and not args.no_resnet else None
     clocks = clk.summary()
@@ -418,7 +478,8 @@ def main():
                 "e2e": {"value": round(world * B / (e2e_ms * 1e-3), 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches * world, "gpu_launches_per_step_per_gpu": launches // args.steps, "roofline": roof, "cpu_baseline": cb, "clocks": clocks,
-                "flops_per_seq": G.e5_flops_per_seq(), "mnist": mnist, "resnet50": resnet}
+                "flops_per_seq": G.e5_flops_per_seq(), "e5_batch32": b32, "gemm_sweep": sweep, "mnist": mnist,
+                "resnet50": resnet}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -232,7 +232,7 @@ int64_t gemm_tc_min_work() {
 
 int gemm_dispatch(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
                   int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
-                  float alpha, float beta, int epi, const float *residual) {
+                  float alpha, float beta, int epi, const float *residual, bool split_k) {
     if (M == 0 || N == 0 || batch == 0) return LONNX_OK;
     if (K == 0) {
         // empty contraction: C = beta*bias (+ epilogue); the SIMT kernel handles it
@@ -261,7 +261,7 @@ int gemm_dispatch(lonnx_ctx *ctx, const float *A, const float *B, const float *b
         const int64_t sW = sB == 0 ? 0 : (int64_t)K * N;
         for (int b = 0; b < batch; ++b) {
             rc = gemm_tc(ctx, A + b * sA, hi + b * sW, lo + b * sW, bias, C + b * sC, M, N, K, K, K, N, alpha, beta,
-                         epi);
+                         epi, true, split_k && batch == 1);
             if (rc == LONNX_E_UNSUPPORTED && b == 0) break;  // fall through to SIMT
             if (rc) return rc;
             if (b == batch - 1) return LONNX_OK;
@@ -284,8 +284,9 @@ LONNX_API int lonnx_gemm_f32(lonnx_ctx *ctx, const float *A, const float *B, con
     if (rc) return rc;
     if (!A || !B || !C || batch < 0 || M < 0 || N < 0 || K < 0 || epilogue < 0 || epilogue > 2)
         return set_error(LONNX_E_BADARG, "gemm: bad arguments");
+    // the single-op entry point may split K when the output has few tiles
     return gemm_dispatch(ctx, A, B, bias, C, batch, M, N, K, strideA, strideB, strideC, transB, alpha,
-                         beta, epilogue, nullptr);
+                         beta, epilogue, nullptr, true);
 }
 
 LONNX_API int lonnx_matmul_f32(lonnx_ctx *ctx, const float *a, const int64_t *as, int ar,

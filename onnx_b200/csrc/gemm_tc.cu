@@ -29,6 +29,7 @@
 #include <cuda.h>
 #include <stdio.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "lonnx_internal.cuh"
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
               const __grid_constant__ CUtensorMap tmWlo, const float *__restrict__ bias, float *__restrict__ C,
               int M, int N, int K, int ldc, float alpha, float beta, int epi, int *dev_flags,
-              const lonnx::ConvArgs cv) {
+              const lonnx::ConvArgs cv, int ksplit, int64_t split_stride) {
     constexpr bool CONV = MODE != MODE_GEMM, RES = MODE == MODE_CONV_RES;
     using G = Cfg<BN, RES>;
     constexpr int S = G::STAGES;
@@ -131,9 +132,18 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     float *sres = reinterpret_cast<float *>(smem + G::RES_OFF);  // [BN][BM] residual tile (RES)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nk = (K + BK - 1) / BK;
+    const int nk_all = (K + BK - 1) / BK;
     const int ntn = (N + BN - 1) / BN, ntiles = ntn * ((M + BM - 1) / BM);
-    const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    // GEMM split-K: CTA b takes tile b / ksplit and that tile's K stages
+    // [ks * chunk, ks * chunk + nk); its raw sums go to C + ks * split_stride
+    const int ks = CONV ? 0 : (int)blockIdx.x % ksplit;
+    const int t0 = CONV ? (int)blockIdx.x : (int)blockIdx.x / ksplit;
+    const int chunk = (nk_all + ksplit - 1) / ksplit;
+    const int nk = CONV ? nk_all : min(chunk, nk_all - ks * chunk);
+    const int kofs = ks * chunk * BK;
+    if (!CONV && ksplit > 1) C += ks * split_stride;
+    const int my_tiles = CONV ? ((int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0)
+                              : (t0 < ntiles && nk > 0 ? 1 : 0);
     const int total = my_tiles * nk;  // (tile, stage) steps of this CTA
     auto tile_n0 = [&](int t) { return (t % ntn) * BN; };
     auto tile_m0 = [&](int t) { return (t / ntn) * BM; };
@@ -198,14 +208,14 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         if (lane == 0) {
             constexpr uint32_t bytes = CONV ? 2 * G::W_TILE : G::STAGE;
             // (tile, K offset) advanced incrementally: no divisions on the issue path
-            int t = (int)blockIdx.x, k0 = 0, s = 0, ph = 0;
+            int t = t0, k0 = 0, s = 0, ph = 0;
             int n0 = tile_n0(t), m0 = tile_m0(t);
             for (int j = 0; j < total && ok; ++j) {
                 if (!mbar_wait(empty(s), ph ^ 1, abort_flag)) { ok = false; break; }
                 mbar_arrive_expect_tx(full(s), bytes);
-                if constexpr (!CONV) tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), k0, m0);
-                tma_load_2d(smem_u32(stageW(s)), &tmW, full(s), k0, n0);
-                tma_load_2d(smem_u32(stageWlo(s)), &tmWlo, full(s), k0, n0);
+                if constexpr (!CONV) tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), kofs + k0, m0);
+                tma_load_2d(smem_u32(stageW(s)), &tmW, full(s), kofs + k0, n0);
+                tma_load_2d(smem_u32(stageWlo(s)), &tmWlo, full(s), kofs + k0, n0);
                 issued = j + 1;
                 if (++s == S) { s = 0; ph ^= 1; }
                 k0 += BK;
@@ -411,7 +421,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::ACC_COL + grp * 64;
         const int rloc = q * 32 + lane;
         for (int tt = 0; tt < my_tiles && ok; ++tt) {
-            const int t = (int)blockIdx.x + tt * (int)gridDim.x, n0 = tile_n0(t), m0 = tile_m0(t);
+            const int t = t0 + tt * (int)gridDim.x, n0 = tile_n0(t), m0 = tile_m0(t);
             if constexpr (RES) {
                 // this thread's residual row (its pixel, its 64 channels) into
                 // shared memory now; only this thread reads it back, after a
@@ -629,7 +639,7 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
 template <int BN, int MODE>
 int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, const CUtensorMap &mwlo,
               const float *bias, float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi,
-              const lonnx::ConvArgs &cv) {
+              const lonnx::ConvArgs &cv, int ksplit = 1, int64_t split_stride = 0) {
     using G = Cfg<BN, MODE == MODE_CONV_RES>;
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {
@@ -640,13 +650,32 @@ int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, cons
     const int64_t tiles = (int64_t)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
     if (tiles >= (1ll << 31)) return lonnx::set_error(LONNX_E_UNSUPPORTED, "gemm_tc: too many tiles");
     // the NCHW (conv) epilogue needs no shared memory: one persistent CTA per SM
-    const int64_t grid = MODE != MODE_GEMM && tiles > ctx->num_sms ? ctx->num_sms : tiles;
+    const int64_t grid = MODE != MODE_GEMM ? (tiles > ctx->num_sms ? ctx->num_sms : tiles) : tiles * ksplit;
     // the tap table (the tail of shared memory) exists only for the implicit conv
     const int smem = MODE != MODE_GEMM ? G::SMEM : G::TAB_OFF + 1024;
     k_gemm_tf32x3<BN, MODE><<<(unsigned)grid, kThreads, smem, ctx->stream>>>(ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi,
-                                                                ctx->dev_flags, cv);
+                                                                ctx->dev_flags, cv, ksplit, split_stride);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
+}
+
+// Split-K finish: C = act(alpha * sum_s ws[s] + beta * bias), the partial
+// tiles summed in split order (deterministic), one pass over the workspace.
+__global__ void k_splitk_reduce(const float *__restrict__ ws, int splits, int64_t stride, int M, int N, int ldc,
+                                const float *__restrict__ bias, float alpha, float beta, int epi,
+                                float *__restrict__ C) {
+    const int64_t total = (int64_t)M * N;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += step) {
+        float x = ws[i];
+        for (int sp = 1; sp < splits; ++sp) x = __fadd_rn(x, ws[sp * stride + i]);
+        const int m = (int)(i / N), n = (int)(i - (int64_t)m * N);
+        if (alpha != 1.0f) x = __fmul_rn(x, alpha);
+        if (bias) x = __fadd_rn(x, beta == 1.0f ? bias[n] : __fmul_rn(beta, bias[n]));
+        if (epi == LONNX_EPI_RELU) x = x > 0.0f ? x : 0.0f;
+        else if (epi == LONNX_EPI_GELU_ERF) x = lonnx_gelu_chain(x);
+        C[(int64_t)m * ldc + n] = x;
+    }
 }
 
 // Tile width for N: 192 or 128, whichever divides N, else the one with the
@@ -680,7 +709,8 @@ int pick_bn_conv(int M, bool res) {
 namespace lonnx {
 
 int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, const float *bias, float *C, int M,
-            int N, int K, int lda, int ldw, int ldc, float alpha, float beta, int epi, bool allow_scratch) {
+            int N, int K, int lda, int ldw, int ldc, float alpha, float beta, int epi, bool allow_scratch,
+            bool split_k) {
     auto al16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
     if (!Wlo) return set_error(LONNX_E_UNSUPPORTED, "gemm_tc: weight must be pre-split");
     if (M <= 0 || N <= 0 || K <= 0 || (lda & 3) || (ldw & 3) || !al16(A) || !al16(Whi) || !al16(Wlo))
@@ -693,8 +723,40 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
     if (rc) return rc;
     rc = make_map(&mwlo, Wlo, N, K, ldw, bn);
     if (rc) return rc;
-    (void)allow_scratch;  // this path allocates nothing
     const ConvArgs none{};
+    // too few output tiles to fill the SMs: split K (each split >= 3 stages,
+    // at most 16), partial tiles into a workspace, then a fixed-order sum.
+    // Needs a device allocation; only when the caller asks for it (split_k).
+    const int64_t tiles = (int64_t)((N + bn - 1) / bn) * ((M + BM - 1) / BM);
+    const int nk = (K + BK - 1) / BK;
+    int ksplit = 1;
+    if (split_k && allow_scratch && tiles * 2 <= ctx->num_sms) {
+        ksplit = (int)(ctx->num_sms / tiles);
+        ksplit = std::min(ksplit, std::min(nk / 3, 16));
+        if (ksplit > 1) ksplit = std::min(ksplit, nk);  // every split gets at least one stage
+        while (ksplit > 1 && (ksplit - 1) * ((nk + ksplit - 1) / ksplit) >= nk) --ksplit;
+    }
+    if (ksplit > 1) {
+        const int64_t stride = (int64_t)M * N;
+        void *ws = nullptr;
+        rc = ctx_alloc(ctx, (size_t)ksplit * stride * 4, &ws);
+        if (rc) return rc;
+        float *w = (float *)ws;
+        rc = bn == 192 ? launch_tc<192, MODE_GEMM>(ctx, ma, mw, mwlo, nullptr, w, M, N, K, N, 1.0f, 1.0f,
+                                                   LONNX_EPI_NONE, none, ksplit, stride)
+                       : launch_tc<128, MODE_GEMM>(ctx, ma, mw, mwlo, nullptr, w, M, N, K, N, 1.0f, 1.0f,
+                                                   LONNX_EPI_NONE, none, ksplit, stride);
+        if (rc == LONNX_OK) {
+            int64_t blocks = (stride + 255) / 256;
+            if (blocks > (int64_t)ctx->num_sms * 8) blocks = (int64_t)ctx->num_sms * 8;
+            k_splitk_reduce<<<(int)blocks, 256, 0, ctx->stream>>>(w, ksplit, stride, M, N, ldc, bias, alpha, beta,
+                                                                 epi, C);
+            rc = cudaGetLastError() == cudaSuccess ? LONNX_OK : set_error(LONNX_E_CUDA, "split-K reduce launch");
+            if (rc == LONNX_OK) ctx->launches++;
+        }
+        ctx_free(ctx, ws);
+        return rc;
+    }
     if (bn == 192) return launch_tc<192, MODE_GEMM>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
     return launch_tc<128, MODE_GEMM>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
 }

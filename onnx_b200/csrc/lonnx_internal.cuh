@@ -74,15 +74,19 @@ int device_guard(lonnx_ctx *ctx);
 // kernels implemented in other translation units (device pointers, ctx stream)
 int gemm_dispatch(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
                   int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
-                  float alpha, float beta, int epi, const float *residual);
+                  float alpha, float beta, int epi, const float *residual, bool split_k = false);
 // Tensor-core GEMM: C = A . W^T with the weight pre-split into Whi, Wlo,
 // both K-major ([N, K] row-major, see split_tf32_nk).  Returns
 // LONNX_E_UNSUPPORTED when the operands do not fit its constraints.
 // allow_scratch = false keeps the call free of device allocation (the
-// activation split then happens inside the kernel).
+// activation split then happens inside the kernel).  split_k lets a call
+// with too few output tiles split K across CTAs (workspace + fixed-order
+// sum): deterministic for a shape, but the summation order then depends on
+// M, so the graph executor (whose batch-sharded rows must not depend on the
+// batch) never asks for it; the single-op Gemm entry point does.
 int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, const float *bias,
             float *C, int M, int N, int K, int lda, int ldw, int ldc, float alpha, float beta,
-            int epi, bool allow_scratch = true);
+            int epi, bool allow_scratch = true, bool split_k = false);
 // Weight [K, N] (trans = 0) or [N, K] (trans = 1) -> hi, lo [N, K]:
 // hi = w with the low 13 mantissa bits cleared, lo = w - hi (exact).
 int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, int N, int trans);

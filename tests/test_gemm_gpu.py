@@ -148,3 +148,23 @@ def test_tf32_operand_truncation(ctx):
     got = _gemm(ctx, A, np.ascontiguousarray(B.T), transB=1)
     rel = np.abs(got - ref).max() / np.abs(ref).max()
     assert rel < 2e-6, rel
+
+
+@pytest.mark.parametrize("epi", [0, 1, 2])
+def test_gemm_split_k_epilogue(ctx, epi):
+    """Few output tiles (M = 256, N = 200 -> 4 tiles) with a long K take the
+    split-K path: partial tiles in a workspace, summed in split order, then
+    alpha, beta * bias and the activation -- against float64."""
+    import math
+    rng = np.random.default_rng(17 + epi)
+    M, K, N = 256, 3072, 200
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    W = (rng.uniform(-1, 1, (N, K)) * 0.05).astype(np.float32)
+    b = rng.uniform(-1, 1, N).astype(np.float32)
+    y = 0.5 * (A.astype(np.float64) @ W.T.astype(np.float64)) + 2.0 * b
+    if epi == 1:
+        y = np.maximum(y, 0)
+    elif epi == 2:
+        y = 0.5 * y * (1 + np.vectorize(math.erf)(y / math.sqrt(2)))
+    got = _gemm(ctx, A, W, b, transB=1, epi=epi, alpha=0.5, beta=2.0)
+    close(got, y.astype(np.float32))
