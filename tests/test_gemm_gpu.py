@@ -168,3 +168,35 @@ def test_gemm_split_k_epilogue(ctx, epi):
         y = 0.5 * y * (1 + np.vectorize(math.erf)(y / math.sqrt(2)))
     got = _gemm(ctx, A, W, b, transB=1, epi=epi, alpha=0.5, beta=2.0)
     close(got, y.astype(np.float32))
+
+
+def test_gemm_cta_pair_kernel_vs_fp64():
+    """The CTA-pair (cta_group::2) GEMM kernel, opt-in via LONNX_GEMM_PAIR=1,
+    run in a child process (the switch is read once per process) on an
+    encoder shape and a ragged one, against float64."""
+    import os
+    import subprocess
+    import sys
+    code = r'''
+import numpy as np, sys
+sys.path.insert(0, %r)
+from onnx_b200.tensor import Context, DeviceTensor
+from onnx_b200 import _native as N
+ctx = Context(0)
+for (M, K, N_, tb) in [(1024, 384, 1536, 1), (700, 520, 200, 0)]:
+    rng = np.random.default_rng(M)
+    A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    B = rng.uniform(-1, 1, (N_, K) if tb else (K, N_)).astype(np.float32)
+    b = rng.uniform(-1, 1, N_).astype(np.float32)
+    ref = A.astype(np.float64) @ (B.T if tb else B).astype(np.float64) + b
+    dA, dB, db = (DeviceTensor.from_host(ctx, x) for x in (A, B, b))
+    y = DeviceTensor(ctx, (M, N_), np.float32)
+    N.check(N.lib.lonnx_gemm_f32(ctx.handle, dA.ptr, dB.ptr, db.ptr, y.ptr, 1, M, N_, K, 0, 0, 0, tb, 1.0, 1.0, 0))
+    ctx.sync()
+    err = np.abs(y.to_host() - ref) - (1e-4 + 1e-4 * np.abs(ref))
+    assert err.max() <= 0, (M, K, N_, float(err.max()))
+print("ok")
+''' % os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, LONNX_GEMM_PAIR="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
