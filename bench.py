@@ -168,6 +168,87 @@ def gemm_sweep(ctx, st, torch, reps=10):
                                                  "(3xTF32 issues 3 MMAs per product)", "cases": out}
 
 
+def bandwidth_kernels(ctx, st, torch, reps=10, scale=1):
+    """Live HBM roofline of every bandwidth-bound kernel through its C-ABI
+    entry point, CUDA events on the launching stream, warm.  Every case moves
+    far more than the 126 MB L2 per launch (scale=1: 400 MB per activation
+    tensor), so back-to-back launches re-read from HBM.  `bytes` is the
+    algorithmic traffic per launch (each operand read once, result written
+    once); frac is against the measured copy bandwidth.  scale < 1 gives the
+    small profiler case (same kernels, 1/4 of the bytes at 0.25)."""
+    import ctypes
+    from onnx_b200 import _native as Nn
+    from onnx_b200.tensor import DeviceTensor
+    hbm, _, kind = peaks()
+    rng = np.random.default_rng(11)
+    H = 384
+    R = int(262144 * scale)
+    i64 = lambda v: (ctypes.c_int64 * len(v))(*v)
+    dev = lambda shape: DeviceTensor(ctx, shape, np.float32)
+
+    def fill(t):
+        Nn.check(Nn.lib.lonnx_memset(ctx.handle, t.ptr, 0x3c, t.nbytes))  # 0x3c3c3c3c ~ 0.0115f
+        return t
+
+    def timed(name, kernel, nbytes, f):
+        for _ in range(3):
+            f()
+        ctx.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            f()
+        e1.record(st)
+        e1.synchronize()
+        ctx.sync()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        gbs = nbytes / (us * 1e-6) / 1e9
+        return {"case": name, "kernel": kernel, "bytes": int(nbytes), "us": round(us, 1), "gbs": round(gbs, 1),
+                "frac": round(gbs / hbm, 4)}
+
+    out = []
+    n = R * H
+    x, r, y = fill(dev((R, H))), fill(dev((R, H))), dev((R, H))
+    gam = DeviceTensor.from_host(ctx, rng.uniform(0.5, 1.5, H).astype(np.float32))
+    bet = DeviceTensor.from_host(ctx, rng.uniform(-0.1, 0.1, H).astype(np.float32))
+    out.append(timed(f"residual+LayerNorm [{R},{H}]", "k_layernorm<12>", 3 * n * 4 + 2 * H * 4,
+                     lambda: Nn.check(Nn.lib.lonnx_layernorm_f32(ctx.handle, x.ptr, r.ptr, gam.ptr, bet.ptr, 1e-12,
+                                                                 y.ptr, R, H))))
+    sh, shb = i64([R, H]), i64([H])
+    out.append(timed(f"Add [{R},{H}]+[{R},{H}]", "k_binary_same<Add>", 3 * n * 4,
+                     lambda: Nn.check(Nn.lib.lonnx_binary_f32(ctx.handle, 0, x.ptr, sh, 2, r.ptr, sh, 2, y.ptr))))
+    out.append(timed(f"Add [{R},{H}]+[{H}] (bias)", "k_binary_rowbcast<Add>", 2 * n * 4 + H * 4,
+                     lambda: Nn.check(Nn.lib.lonnx_binary_f32(ctx.handle, 0, x.ptr, sh, 2, gam.ptr, shb, 1, y.ptr))))
+    out.append(timed(f"Relu [{n}]", "k_unary<Relu>", 2 * n * 4,
+                     lambda: Nn.check(Nn.lib.lonnx_unary_f32(ctx.handle, 0, x.ptr, y.ptr, n))))
+    out.append(timed(f"Erf-GELU [{n}]", "k_unary<GELU>", 2 * n * 4,
+                     lambda: Nn.check(Nn.lib.lonnx_unary_f32(ctx.handle, 4, x.ptr, y.ptr, n))))
+    out.append(timed(f"Softmax [{n // 128},128]", "k_softmax_lastdim<4>", 2 * n * 4,
+                     lambda: Nn.check(Nn.lib.lonnx_softmax_f32(ctx.handle, x.ptr, y.ptr, n // 128, 128, 1))))
+    red = dev((R,))
+    ax = i64([1])
+    out.append(timed(f"ReduceMean [{R},{H}] axis -1", "k_reduce_rows", n * 4 + R * 4,
+                     lambda: Nn.check(Nn.lib.lonnx_reduce_f32(ctx.handle, 2, x.ptr, sh, 2, ax, 1, red.ptr))))
+    B4 = R // 128
+    tsh, perm = i64([B4, 128, 12, 32]), i64([0, 2, 1, 3])
+    out.append(timed(f"Transpose [{B4},128,12,32] (0,2,1,3)", "k_transpose", 2 * n * 4,
+                     lambda: Nn.check(Nn.lib.lonnx_transpose(ctx.handle, x.ptr, 4, tsh, 4, perm, y.ptr))))
+    del r, red
+    V = 250037
+    table = fill(dev((V, H)))
+    ids = DeviceTensor.from_host(ctx, rng.integers(0, V, R).astype(np.int64))
+    out.append(timed(f"Gather [{V},{H}] x {R} ids", "k_gather_rows<uint4>", 2 * n * 4 + R * 8,
+                     lambda: Nn.check(Nn.lib.lonnx_gather(ctx.handle, table.ptr, 4, 1, V, H, ids.ptr, R, y.ptr))))
+    del table, ids, x, y
+    Np, C, Hp = max(1, int(64 * scale)), 64, 112
+    xp, yp = fill(dev((Np, C, Hp, Hp))), dev((Np, C, 56, 56))
+    out.append(timed(f"MaxPool 3x3/2 [{Np},{C},{Hp},{Hp}]", "k_maxpool2d", (Np * C * Hp * Hp + Np * C * 56 * 56) * 4,
+                     lambda: Nn.check(Nn.lib.lonnx_maxpool2d_f32(ctx.handle, xp.ptr, yp.ptr, Np, C, Hp, Hp, 3, 3, 2, 2,
+                                                                 1, 1, 56, 56))))
+    return {"peak_gbs": hbm, "peak_note": f"{kind} HBM copy bandwidth", "l2": "every launch moves >> 126 MB L2",
+            "cases": out}
+
+
 def e5_batch(ctx, st, torch, cg, vocab, batch=32, reps=10):
     """the same encoder at batch 32, device-resident inputs."""
     from onnx_b200 import graphs as G
@@ -364,6 +445,10 @@ def main():
                     help="time one Conv through the C-ABI and exit (for profiler captures)")
     ap.add_argument("--roofline-case", action="store_true",
                     help="run only the roofline GEMM (FFN1 shape) and exit (for ncu captures)")
+    ap.add_argument("--bw-case", action="store_true",
+                    help="run only the bandwidth-kernel sweep at 1/4 size and exit (for ncu captures)")
+    ap.add_argument("--bw-only", action="store_true",
+                    help="print only the full-size bandwidth-kernel sweep and exit")
     ap.add_argument("--profile-case", type=int, default=0, metavar="B",
                     help="run two 2-layer e5 forwards at batch B and exit (small case for ncu captures)")
     args = ap.parse_args()
@@ -382,6 +467,13 @@ def main():
         ctx = Context(0)
         print(json.dumps(resnet_throughput(ctx, torch.cuda.ExternalStream(ctx.stream), torch, batch=args.resnet_case,
                                            reps=2)))
+        return
+    if args.bw_case or args.bw_only:
+        import torch
+        from onnx_b200.tensor import Context
+        ctx = Context(0)
+        print(json.dumps(bandwidth_kernels(ctx, torch.cuda.ExternalStream(ctx.stream), torch,
+                                           reps=3 if args.bw_case else 10, scale=0.25 if args.bw_case else 1)))
         return
     if args.roofline_case:
         import torch
@@ -461,6 +553,7 @@ def main():
     b32 = e5_batch(ctx, st, torch, cg, args.vocab) if rank == 0 else None
     mnist = mnist_latency(ctx, st, torch) if rank == 0 else None
     resnet = resnet_throughput(ctx, st, torch) if rank == 0 and not args.no_resnet else None
+    bw = bandwidth_kernels(ctx, st, torch) if rank == 0 else None
     clocks = clk.summary()
     if rank == 0:
         cb = None if args.no_cpu_baseline else cpu_baseline(8)
@@ -479,7 +572,7 @@ def main():
                         "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches * world, "gpu_launches_per_step_per_gpu": launches // args.steps, "roofline": roof, "cpu_baseline": cb, "clocks": clocks,
                 "flops_per_seq": G.e5_flops_per_seq(), "e5_batch32": b32, "gemm_sweep": sweep, "mnist": mnist,
-                "resnet50": resnet}
+                "resnet50": resnet, "bandwidth_kernels": bw}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

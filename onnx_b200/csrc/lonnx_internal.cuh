@@ -129,22 +129,38 @@ int gemm_simt(lonnx_ctx *ctx, const float *A, const float *B, const float *bias,
 __device__ __forceinline__ float lonnx_erf_as(float x) {
     const float a1 = 0.254829592f, a2 = -0.284496736f, a3 = 1.421413741f;
     const float a4 = -1.453152027f, a5 = 1.061405429f, p = 0.3275911f;
-    const float s = x < 0.0f ? -1.0f : 1.0f;
+    const unsigned neg = x < 0.0f ? 0x80000000u : 0u;  // s * y with s = -1 is an exact negation
     x = fabsf(x);
-    const float t = __fdiv_rn(1.0f, __fadd_rn(1.0f, __fmul_rn(p, x)));
+    const float t = __frcp_rn(__fadd_rn(1.0f, __fmul_rn(p, x)));  // == RN(1 / d), as 1.0f / d
     float poly = __fadd_rn(__fmul_rn(a5, t), a4);
     poly = __fadd_rn(__fmul_rn(poly, t), a3);
     poly = __fadd_rn(__fmul_rn(poly, t), a2);
     poly = __fadd_rn(__fmul_rn(poly, t), a1);
     const float e = expf(__fmul_rn(-x, x));
     const float y = __fsub_rn(1.0f, __fmul_rn(__fmul_rn(poly, t), e));
-    return s * y;
+    return __uint_as_float(__float_as_uint(y) ^ neg);
 }
 
 // GELU as the exported node chain computes it: Div(x, sqrt 2) -> Erf ->
 // Add(1) -> Mul(x) -> Mul(0.5), each step rounded to float.
+// x / fl(sqrt 2) correctly rounded.  For 2^-100 < |x| < inf one Markstein
+// correction step of q0 = x * RN(1/c) gives the correctly rounded quotient
+// (P. Markstein, "IA-64 and elementary functions", 2000: the remainder
+// x - q0*c is exact in an FMA, then q = q0 + rem * RN(1/c)); this was
+// checked against IEEE float division for every finite float.  Tiny,
+// subnormal and non-finite x take the ordinary division.
+__device__ __forceinline__ float lonnx_div_sqrt2(float x) {
+    const float c = 1.41421353816986083984375f;
+    const float r = 0.707106769084930419921875f;  // RN(1 / c)
+    const float ax = fabsf(x);
+    if (!(ax > 0x1p-100f && ax < INFINITY)) return __fdiv_rn(x, c);
+    const float q0 = __fmul_rn(x, r);
+    const float rem = __fmaf_rn(-q0, c, x);
+    return __fmaf_rn(rem, r, q0);
+}
+
 __device__ __forceinline__ float lonnx_gelu_chain(float x) {
-    const float a = __fdiv_rn(x, 1.41421353816986083984375f);
+    const float a = lonnx_div_sqrt2(x);
     const float e = lonnx_erf_as(a);
     const float c = __fadd_rn(e, 1.0f);
     return __fmul_rn(__fmul_rn(x, c), 0.5f);

@@ -7,6 +7,8 @@
 // thread per output column so that the loads stay coalesced.
 #include <float.h>
 
+#include <algorithm>
+
 #include "lonnx_internal.cuh"
 
 namespace {
@@ -219,24 +221,43 @@ __global__ void k_reduce_mid(int op, const float *__restrict__ x, float *__restr
 
 // ---------------------------------------------------------------------------
 // MaxPool2D (TensorOps.cs:1025-1099): window clipped to the input, max from
-// -inf; the window ignores dilation as the reference's does.
-__global__ void k_maxpool2d(const float *__restrict__ x, float *__restrict__ y, int N, int C,
-                            int H, int W, int kh, int kw, int sh, int sw, int pt, int pl, int Ho,
-                            int Wo) {
-    const int64_t total = (int64_t)N * C * Ho * Wo;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += stride) {
-        const int ox = (int)(t % Wo);
-        const int oy = (int)((t / Wo) % Ho);
-        const int64_t nc = t / ((int64_t)Wo * Ho);
+// -inf; the window ignores dilation as the reference's does.  blockIdx.y
+// walks the (n, c) planes and x the output pixels of a plane, so the index
+// arithmetic is one 32-bit division per output (a flat 64-bit index with
+// three 64-bit divisions made this kernel instruction-bound at 29% of HBM).
+// KH = KW = 0: runtime window; otherwise the window is unrolled and all its
+// loads are issued before the max (predicated on the clipped window), so a
+// thread has KH*KW loads in flight instead of one.
+template <int KH, int KW>
+__global__ void k_maxpool2d(const float *__restrict__ x, float *__restrict__ y, int64_t planes, int H,
+                            int W, int kh, int kw, int sh, int sw, int pt, int pl, int Ho, int Wo) {
+    if (KH > 0) { kh = KH; kw = KW; }
+    const int per_plane = Ho * Wo;
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= per_plane) return;
+    const int oy = t / Wo, ox = t - oy * Wo;
+    const int r0 = oy * sh - pt, c0 = ox * sw - pl;
+    const int rmin = max(r0, 0), rmax = min(r0 + kh, H);
+    const int cmin = max(c0, 0), cmax = min(c0 + kw, W);
+    for (int64_t nc = blockIdx.y; nc < planes; nc += gridDim.y) {
         const float *xp = x + nc * H * W;
-        const int r0 = oy * sh - pt, c0 = ox * sw - pl;
-        const int rmin = max(r0, 0), rmax = min(r0 + kh, H);
-        const int cmin = max(c0, 0), cmax = min(c0 + kw, W);
         float m = -INFINITY;
-        for (int r = rmin; r < rmax; ++r)
-            for (int c = cmin; c < cmax; ++c) m = fmaxf(m, xp[(int64_t)r * W + c]);
-        y[t] = m;
+        if (KH > 0) {
+            float v[KH * KW > 0 ? KH * KW : 1];
+#pragma unroll
+            for (int i = 0; i < KH; ++i)
+#pragma unroll
+                for (int j = 0; j < KW; ++j) {
+                    const int r = r0 + i, c = c0 + j;
+                    v[i * KW + j] = (r >= 0 && r < H && c >= 0 && c < W) ? __ldg(xp + r * W + c) : -INFINITY;
+                }
+#pragma unroll
+            for (int i = 0; i < KH * KW; ++i) m = fmaxf(m, v[i]);
+        } else {
+            for (int r = rmin; r < rmax; ++r)
+                for (int c = cmin; c < cmax; ++c) m = fmaxf(m, __ldg(xp + r * W + c));
+        }
+        y[nc * per_plane + t] = m;
     }
 }
 
@@ -360,7 +381,20 @@ LONNX_API int lonnx_maxpool2d_f32(lonnx_ctx *ctx, const float *x, float *y, int 
     if (!x || !y || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0) return set_error(LONNX_E_BADARG, "maxpool: bad arguments");
     const int64_t total = (int64_t)N * C * Ho * Wo;
     if (total <= 0) return LONNX_OK;
-    k_maxpool2d<<<grid_for(ctx, total), 256, 0, ctx->stream>>>(x, y, N, C, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
+    if ((int64_t)H * W >= ((int64_t)1 << 31) || (int64_t)Ho * Wo >= ((int64_t)1 << 31))
+        return set_error(LONNX_E_UNSUPPORTED, "maxpool: plane of more than 2^31 elements");
+    const int64_t planes = (int64_t)N * C;
+    const int per_plane = Ho * Wo;
+    // about 16 blocks per SM in all; each thread then walks several planes
+    const int64_t bx = (per_plane + 255) / 256;
+    const int64_t by = std::max<int64_t>(1, std::min<int64_t>({planes, 65535, ((int64_t)ctx->num_sms * 16 + bx - 1) / bx}));
+    const dim3 grid((unsigned)bx, (unsigned)by);
+    if (kh == 3 && kw == 3)
+        k_maxpool2d<3, 3><<<grid, 256, 0, ctx->stream>>>(x, y, planes, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
+    else if (kh == 2 && kw == 2)
+        k_maxpool2d<2, 2><<<grid, 256, 0, ctx->stream>>>(x, y, planes, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
+    else
+        k_maxpool2d<0, 0><<<grid, 256, 0, ctx->stream>>>(x, y, planes, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
 }

@@ -167,3 +167,64 @@ def test_sharded_rank_failure_is_detected_gloo():
             p.kill()
     assert res[1] == "RuntimeError"
     assert res[0] != "finished"
+
+
+_DIV_SQRT2_C = r"""
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+/* The device helper lonnx_div_sqrt2 (onnx_b200/csrc/lonnx_internal.cuh),
+   restated with libm's correctly rounded fmaf: counts the inputs among
+   `count` bit patterns (start, start+step, ...) whose result differs from
+   IEEE float division by fl(sqrt 2). */
+static float div_sqrt2(float x) {
+    const float c = 1.41421353816986083984375f, r = 0.707106769084930419921875f;
+    const float ax = fabsf(x);
+    if (!(ax > 0x1p-100f && ax < INFINITY)) return x / c;
+    const float q0 = x * r;
+    const float rem = fmaf(-q0, c, x);
+    return fmaf(rem, r, q0);
+}
+long long mismatches(uint32_t start, uint32_t step, long long count) {
+    long long bad = 0;
+    uint32_t u = start;
+    for (long long i = 0; i < count; ++i, u += step) {
+        float x, q, ref;
+        memcpy(&x, &u, 4);
+        if (x != x) continue;
+        volatile float c = 1.41421353816986083984375f;
+        ref = x / c;
+        q = div_sqrt2(x);
+        uint32_t a, b;
+        memcpy(&a, &ref, 4);
+        memcpy(&b, &q, 4);
+        bad += a != b;
+    }
+    return bad;
+}
+"""
+
+
+def test_div_sqrt2_correctly_rounded(tmp_path):
+    """The GELU chain's x / fl(sqrt 2) uses one Markstein correction step
+    instead of a division; it must equal IEEE division bit for bit.  Every
+    float in [1, 2) and [2^-100, 2^-99) plus a strided sample of all 2^32
+    patterns (the full range was checked exhaustively when the helper was
+    written)."""
+    import ctypes
+    import shutil
+    import subprocess
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not available")
+    src = tmp_path / "d.c"
+    src.write_text(_DIV_SQRT2_C)
+    so = tmp_path / "d.so"
+    subprocess.run(["gcc", "-O2", "-ffp-contract=off", "-shared", "-fPIC", "-o", str(so), str(src), "-lm"],
+                   check=True)
+    lib = ctypes.CDLL(str(so))
+    lib.mismatches.restype = ctypes.c_longlong
+    lib.mismatches.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_longlong]
+    assert lib.mismatches(0x3F800000, 1, 1 << 23) == 0
+    assert lib.mismatches(0x0D800000, 1, 1 << 23) == 0  # 2^-100 .. 2^-99
+    assert lib.mismatches(0x80000000, 1, 1 << 23) == 0  # negative subnormals and tiny
+    assert lib.mismatches(7, 997, (1 << 32) // 997) == 0

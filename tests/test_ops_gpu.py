@@ -218,6 +218,72 @@ def test_transpose_bit_exact(P, shape, perm):
     assert np.array_equal(ok(P.Transpose(x, perm)), O.transpose(x, perm))
 
 
+_TRANSPOSE_CASES = [((2, 128, 12, 32), [0, 2, 1, 3]), ((2, 128, 12, 32), [0, 2, 3, 1]), ((33, 65), [1, 0]),
+                    ((1, 5, 1, 7), [3, 2, 1, 0]), ((4, 5, 6), [0, 1, 2]), ((2, 1, 3), [2, 1, 0]),
+                    ((3, 40, 7, 33), [1, 3, 0, 2]), ((2, 3, 4, 5, 6, 7), [5, 4, 3, 2, 1, 0]),
+                    ((2, 2, 2, 2, 2, 2, 2, 3), [7, 6, 5, 4, 3, 2, 1, 0]), ((6, 4, 5, 3), [0, 1, 3, 2]),
+                    ((7, 9, 3), [1, 0, 2])]
+
+
+@pytest.mark.parametrize("dtype", [np.float32, np.uint8, np.int16, np.float64])
+@pytest.mark.parametrize("shape,perm", _TRANSPOSE_CASES)
+def test_transpose_c_abi_all_element_sizes(ctx, shape, perm, dtype):
+    """lonnx_transpose for 1/2/4/8-byte elements: run copies (innermost axis
+    kept, vectorised), 32x32 shared-memory tiles (innermost axis moved), size-1
+    dimensions and merged adjacent dimensions, an identity permutation; bit-exact."""
+    import ctypes
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    x = (np.random.default_rng(len(shape)).standard_normal(shape) * 100).astype(dtype)
+    dx = DeviceTensor.from_host(ctx, x)
+    ref = np.ascontiguousarray(np.transpose(x, perm))
+    dy = DeviceTensor(ctx, ref.shape, dtype)
+    sh = (ctypes.c_int64 * len(shape))(*shape)
+    pm = (ctypes.c_int64 * len(perm))(*perm)
+    N.check(N.lib.lonnx_transpose(ctx.handle, dx.ptr, x.itemsize, sh, len(shape), pm, dy.ptr))
+    ctx.sync()
+    assert np.array_equal(dy.to_host(), ref)
+
+
+def test_maxpool_many_planes_and_resnet_shape(P):
+    """More (n, c) planes than one grid dimension holds, and ResNet-50's
+    3x3/2 pad-1 pool; bit-exact against the oracle."""
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((2, 40000, 3, 3)).astype(np.float32)
+    got = ok(P.MaxPool(x, auto_pad="NOTSET", kernel_shape=[2, 2], pads=[0, 0, 0, 0], strides=[1, 1]))
+    assert np.array_equal(got, O.maxpool(x, auto_pad="NOTSET", kernel_shape=[2, 2], pads=[0, 0, 0, 0],
+                                         strides=[1, 1]))
+    x = rng.standard_normal((2, 8, 112, 112)).astype(np.float32)
+    got = ok(P.MaxPool(x, auto_pad="NOTSET", kernel_shape=[3, 3], pads=[1, 1, 1, 1], strides=[2, 2]))
+    assert np.array_equal(got, O.maxpool(x, auto_pad="NOTSET", kernel_shape=[3, 3], pads=[1, 1, 1, 1],
+                                         strides=[2, 2]))
+
+
+def test_gelu_unary_matches_node_chain(ctx):
+    """The fused Erf-GELU (lonnx_unary_f32 op 4) against the exported node
+    chain Div(sqrt 2) -> Erf -> Add(1) -> Mul(x) -> Mul(0.5) on the oracle,
+    over a wide range including tiny, subnormal, huge and infinite inputs.
+    Erf's exp differs from the host's by an ulp, hence the Erf tolerance."""
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    rng = np.random.default_rng(9)
+    x = np.concatenate([rng.uniform(-6, 6, 1 << 16), rng.standard_normal(4096) * 1e-30,
+                        np.array([0.0, -0.0, 1e-45, -1e-45, 1e-38, 3e38, -3e38, np.inf, -np.inf, 1.0, -1.0])]
+                       ).astype(np.float32)
+    dx = DeviceTensor.from_host(ctx, x)
+    dy = DeviceTensor(ctx, x.shape, np.float32)
+    N.check(N.lib.lonnx_unary_f32(ctx.handle, 4, dx.ptr, dy.ptr, x.size))
+    ctx.sync()
+    got = dy.to_host()
+    with np.errstate(all="ignore"):
+        a = x / np.float32(1.41421353816986083984375)
+        e = O.unary("Erf", a)
+        ref = ((x * (e + np.float32(1.0))).astype(np.float32) * np.float32(0.5)).astype(np.float32)
+    fin = np.isfinite(ref)
+    close(got[fin], ref[fin], atol=1e-6, rtol=1e-6)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+
+
 def test_reshape_and_unsqueeze(P):
     x = np.arange(24, dtype=np.float32).reshape(2, 3, 4)
     assert ok(P.Reshape(x, np.array([0, -1], np.int64))).shape == (2, 12)
