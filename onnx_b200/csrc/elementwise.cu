@@ -74,6 +74,31 @@ __global__ void k_binary_rowbcast(const float *__restrict__ full, const float *_
     }
 }
 
+// b (or a, when SWAP) is constant along the trailing `inner` elements of
+// the flat output: [.., R, inner] op [.., R, 1..1] (masked mean pooling,
+// unfused LayerNorm Sub/Div by the row statistics).
+template <int OP, bool SWAP>
+__global__ void k_binary_colbcast(const float *__restrict__ full, const float *__restrict__ col,
+                                  float *__restrict__ y, int64_t n, int64_t inner, int vec) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    if (vec) {  // inner % 4 == 0, full and y 16-byte aligned
+        const int64_t n4 = n / 4, in4 = inner / 4;
+        const float4 *f4 = reinterpret_cast<const float4 *>(full);
+        float4 *y4 = reinterpret_cast<float4 *>(y);
+        for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
+            const float4 u = __ldg(f4 + i);
+            const float v = __ldg(col + i / in4);
+            y4[i] = SWAP ? make_float4(binop<OP>(v, u.x), binop<OP>(v, u.y), binop<OP>(v, u.z), binop<OP>(v, u.w))
+                         : make_float4(binop<OP>(u.x, v), binop<OP>(u.y, v), binop<OP>(u.z, v), binop<OP>(u.w, v));
+        }
+        return;
+    }
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += stride) {
+        const float u = full[i], v = col[i / inner];
+        y[i] = SWAP ? binop<OP>(v, u) : binop<OP>(u, v);
+    }
+}
+
 // scalar operand: a op s (or s op a when SWAP)
 template <int OP, bool SWAP>
 __global__ void k_binary_scalar(const float *__restrict__ full, const float *__restrict__ s,
@@ -191,6 +216,39 @@ int launch_binary(lonnx_ctx *ctx, const float *a, const int64_t *as, int ar, con
     }
     if (nb == n && trailing(as, ar, na) && vecok) {
         k_binary_rowbcast<OP, true><<<grid_for(ctx, n / 4 + 1, T), T, 0, st>>>(b, a, y, n, na);
+        LONNX_CHECK_LAUNCH(ctx);
+        return LONNX_OK;
+    }
+    // column broadcast: the small operand's shape is the output's leading
+    // dims followed by 1s; returns the run length it is constant over
+    auto leading = [&](const int64_t *s, int r, int64_t cnt) -> int64_t {
+        if (cnt == n || cnt <= 1 || r > orank) return 0;
+        int last = -1;
+        for (int d = 0; d < orank; ++d) {
+            const int i = d - (orank - r);
+            const int64_t sd = i >= 0 ? s[i] : 1;
+            if (sd != 1) {
+                if (sd != os[d]) return 0;
+                last = d;
+            }
+        }
+        for (int d = 0; d <= last; ++d) {
+            const int i = d - (orank - r);
+            if ((i >= 0 ? s[i] : 1) != os[d]) return 0;
+        }
+        int64_t inner = 1;
+        for (int d = last + 1; d < orank; ++d) inner *= os[d];
+        return inner > 1 && cnt * inner == n ? inner : 0;
+    };
+    if (int64_t inner = na == n ? leading(bs, br, nb) : 0) {
+        const int vec = (inner & 3) == 0 && aligned16(a) && aligned16(y);
+        k_binary_colbcast<OP, false><<<grid_for(ctx, (vec ? n / 4 : n) + 1, T), T, 0, st>>>(a, b, y, n, inner, vec);
+        LONNX_CHECK_LAUNCH(ctx);
+        return LONNX_OK;
+    }
+    if (int64_t inner = nb == n ? leading(as, ar, na) : 0) {
+        const int vec = (inner & 3) == 0 && aligned16(b) && aligned16(y);
+        k_binary_colbcast<OP, true><<<grid_for(ctx, (vec ? n / 4 : n) + 1, T), T, 0, st>>>(b, a, y, n, inner, vec);
         LONNX_CHECK_LAUNCH(ctx);
         return LONNX_OK;
     }

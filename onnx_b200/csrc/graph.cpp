@@ -856,7 +856,28 @@ bool exec_ln_step(lonnx_graph *g, const Step &s) {
     Value x = lookup(g, s.a);
     const Value *r = s.b.empty() ? nullptr : &lookup(g, s.b);
     if (x.dtype != DT_FLOAT || x.shape.empty()) return false;
-    if (r && r->shape != x.shape) return false;
+    if (r && r->dtype != DT_FLOAT) return false;
+    if (r && r->shape != x.shape) {
+        // a broadcasting Add (the embedding sum plus [S, H] position
+        // embeddings): run that Add on its own, then the LayerNorm on its sum
+        int64_t os[8];
+        int orank = 0;
+        if (x.shape.size() > 8 || r->shape.size() > 8 ||
+            lonnx_broadcast_shape(x.shape.data(), (int)x.shape.size(), r->shape.data(), (int)r->shape.size(), os,
+                                  &orank))
+            return false;
+        std::vector<int64_t> bshape(os, os + orank);
+        const Value &gm0 = lookup(g, s.gamma), &bt0 = lookup(g, s.beta);
+        if (bshape.empty() || gm0.numel() != bshape.back() || bt0.numel() != bshape.back()) return false;
+        Value rr = *r;
+        ensure_dev(g, x);
+        ensure_dev(g, rr);
+        Value sum = new_dev(g, DT_FLOAT, bshape);
+        ck(lonnx_binary_f32(g->ctx, LONNX_ADD, (const float *)x.dptr(), x.shape.data(), (int)x.shape.size(),
+                            (const float *)rr.dptr(), rr.shape.data(), (int)rr.shape.size(), (float *)sum.dptr_mut()));
+        x = sum;
+        r = nullptr;
+    }
     const Value &gm = lookup(g, s.gamma), &bt = lookup(g, s.beta);
     const int64_t cols = x.shape.back();
     if (gm.numel() != cols || bt.numel() != cols) return false;

@@ -27,7 +27,8 @@ def ok(r):
 @pytest.mark.parametrize("op", ["Add", "Sub", "Mul", "Div", "Pow"])
 @pytest.mark.parametrize("sa,sb", [((1, 8, 28, 28), (8, 1, 1)), ((64, 384), (384,)), ((384,), (64, 384)),
                                    ((3, 4, 5), ()), ((), (3, 4, 5)), ((2, 12, 16, 16), (2, 1, 1, 16)),
-                                   ((5, 1, 7), (1, 6, 1)), ((37,), (37,))])
+                                   ((5, 1, 7), (1, 6, 1)), ((37,), (37,)), ((4, 16, 384), (4, 16, 1)),
+                                   ((4, 16, 1), (4, 16, 384)), ((3, 5, 6), (3, 1, 1)), ((3, 5, 7), (3, 5, 1))])
 def test_binary_broadcast(P, op, sa, sb):
     rng = np.random.default_rng(hash((op, sa, sb)) % 2**32)
     a = rng.uniform(0.5, 2.0, sa).astype(np.float32)
