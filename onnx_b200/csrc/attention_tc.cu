@@ -227,14 +227,243 @@ k_attention_tc(const float *__restrict__ q, const float *__restrict__ k, const f
     }
 }
 
+// ---------------------------------------------------------------------------
+// k_attention_tc8: the same computation with 8 warps and TMA-fed operands.
+//   1. one thread loads the raw Q, K and V tiles of (b, h) by TMA (128 rows x
+//      32 fp32, 128-byte swizzle, straight into the MMA layout for Q and K;
+//      V lands in the V^T_lo area); all 256 threads then write Q_lo, K_lo in
+//      place beside them and transpose V into V^T, V^T_lo (keys >= S zeroed);
+//   2. S = Q K^T as before;
+//   3. warps w and w + 4 share TMEM lanes 32 (w % 4) .. +31 (one query row
+//      per thread) and split the 128 keys: warp group g takes columns
+//      [64 g, 64 g + 64) for the row max and, in each 64-key half, the 32
+//      keys [64 hf + 32 g, +32) for e = exp(..) -> E; the partial maxima and
+//      sums meet in shared memory;
+//   4. O += E V per half as before; 5. each group stores 16 of the 32 columns.
+// The TMA loads replace 24 dependent 16-byte global loads per thread, which
+// were the kernel's main stall, and the second warp group halves each
+// thread's softmax work.
+constexpr int AT8 = 256;
+constexpr int OFF_RED = OFF_MASK + 128 * 4;          // [2][128] max, [2][128] sum
+constexpr int OFF_BAR8 = OFF_RED + 4 * 128 * 4;
+constexpr int SMEM8 = OFF_BAR8 + 64 + 1024;
+
+__global__ void __launch_bounds__(AT8, 2)
+k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                const __grid_constant__ CUtensorMap tv, const float *__restrict__ maskadd, float *__restrict__ out,
+                int S, int heads, float scale, int *dev_flags) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + OFF_BAR8);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 4);
+    float *msk = reinterpret_cast<float *>(sm + OFF_MASK);
+    float *red_max = reinterpret_cast<float *>(sm + OFF_RED), *red_sum = red_max + 2 * 128;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const int bh = blockIdx.x;
+    const int b = bh / heads, h = bh % heads;
+    const uint32_t bar_ld = smem_u32(bars), bar_s = smem_u32(bars + 1), bar_o = smem_u32(bars + 2),
+                   bar_drain = smem_u32(bars + 3);
+
+    if (t == 0) {
+        mbar_init(bar_ld, 1);
+        mbar_init(bar_s, 1);
+        mbar_init(bar_o, 1);
+        mbar_init(bar_drain, 1);
+        fence_mbar_init();
+        prefetch_tmap(&tq);
+        prefetch_tmap(&tk);
+        prefetch_tmap(&tv);
+        mbar_arrive_expect_tx(bar_ld, 3 * TILE);
+        tma_load_2d(smem_u32(sm + OFF_Q), &tq, bar_ld, h * DH, b * S);
+        tma_load_2d(smem_u32(sm + OFF_K), &tk, bar_ld, h * DH, b * S);
+        tma_load_2d(smem_u32(sm + OFF_VTLO), &tv, bar_ld, h * DH, b * S);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), 256);
+        tmem_relinquish();
+    }
+    if (t < 128) msk[t] = (maskadd && t < S) ? maskadd[(int64_t)b * S + t] : 0.0f;
+    __syncthreads();  // barrier inits visible before anyone waits on them
+    bool ok = mbar_wait(bar_ld, 0, nullptr);
+
+    // ---- 1. lo parts and V^T ----------------------------------------------------
+    {
+        const int row = t & 127, c0 = (t >> 7) * 4;  // this thread: 4 of the row's 8 chunks
+        float4 vr[4];
+        if (ok) {
+#pragma unroll
+            for (int c = c0; c < c0 + 4; ++c) {
+                const int o = swz(row, c);
+                *reinterpret_cast<float4 *>(sm + OFF_QLO + o) = lo4(*reinterpret_cast<const float4 *>(sm + OFF_Q + o));
+                *reinterpret_cast<float4 *>(sm + OFF_KLO + o) = lo4(*reinterpret_cast<const float4 *>(sm + OFF_K + o));
+                vr[c - c0] = *reinterpret_cast<const float4 *>(sm + OFF_VTLO + o);
+            }
+        }
+        __syncthreads();  // every raw V value is in registers before V^T_lo is overwritten
+        if (ok) {
+            const bool live = row < S;
+            const int atom = row >> 5, ch = (row & 31) >> 2, wd = row & 3;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float e4[4] = {vr[c].x, vr[c].y, vr[c].z, vr[c].w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int d = (c0 + c) * 4 + u;
+                    const int off = atom * 32 * ROWB + swz(d, ch) + wd * 4;
+                    const float x = live ? e4[u] : 0.0f;
+                    *reinterpret_cast<float *>(sm + OFF_VT + off) = x;
+                    *reinterpret_cast<float *>(sm + OFF_VTLO + off) = __fsub_rn(x, tf32_hi(x));
+                }
+            }
+        }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // ---- 2. S = Q K^T --------------------------------------------------------------
+    if (t == 0 && ok) {
+        constexpr uint32_t idesc = idesc_tf32(128, 128);
+        const uint32_t a = smem_u32(sm + OFF_Q), al = smem_u32(sm + OFF_QLO);
+        const uint32_t bk = smem_u32(sm + OFF_K), bl = smem_u32(sm + OFF_KLO);
+#pragma unroll
+        for (int kk = 0; kk < DH / 8; ++kk) {
+            const uint32_t ko = kk * 32;
+            mma_tf32(tmem, smem_desc_sw128(al + ko), smem_desc_sw128(bk + ko), idesc, kk != 0);
+            mma_tf32(tmem, smem_desc_sw128(a + ko), smem_desc_sw128(bl + ko), idesc, 1);
+            mma_tf32(tmem, smem_desc_sw128(a + ko), smem_desc_sw128(bk + ko), idesc, 1);
+        }
+        mma_commit(bar_s);
+    }
+    if (ok && !mbar_wait(bar_s, 0, nullptr)) ok = false;
+    tc_fence_after();
+
+    // ---- 3. softmax: two warps per TMEM lane quarter, keys split -------------------
+    const int g = warp >> 2, row = (warp & 3) * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const float inv_scale = 1.0f / scale;
+    float mx = 0.0f;
+    if (ok) {
+#pragma unroll
+        for (int c = 2 * g; c < 2 * g + 2; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(lane_addr + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int key = c * 32 + j;
+                if (key < S) mx = fmaxf(mx, __uint_as_float(r[j]) * inv_scale + msk[key]);
+            }
+        }
+    }
+    red_max[g * 128 + row] = mx;
+    __syncthreads();
+    mx = fmaxf(red_max[row], red_max[128 + row]);
+    float sum = 0.0f;
+    for (int hf = 0; hf < 2; ++hf) {
+        if (ok) {
+            const int c = hf * 2 + g;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(lane_addr + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) {
+                float e[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int key = c * 32 + ch * 4 + u;
+                    e[u] = key < S ? expf(__uint_as_float(r[ch * 4 + u]) * inv_scale + msk[key] - mx) : 0.0f;
+                    sum += e[u];
+                }
+                const float4 ev = make_float4(e[0], e[1], e[2], e[3]);
+                *reinterpret_cast<float4 *>(sm + OFF_E + g * TILE + swz(row, ch)) = ev;
+                *reinterpret_cast<float4 *>(sm + OFF_ELO + g * TILE + swz(row, ch)) = lo4(ev);
+            }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        if (t == 0 && ok) {
+            constexpr uint32_t idesc = idesc_tf32(128, DH);
+            const uint32_t oacc = tmem + 128;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t atom = kk >> 2, ko = (kk & 3) * 32, vatom = hf * 2 + atom;
+                const uint32_t a = smem_u32(sm + OFF_E + atom * TILE) + ko, al = smem_u32(sm + OFF_ELO + atom * TILE) + ko;
+                const uint32_t bv = smem_u32(sm + OFF_VT + vatom * 32 * ROWB) + ko;
+                const uint32_t bl = smem_u32(sm + OFF_VTLO + vatom * 32 * ROWB) + ko;
+                mma_tf32(oacc, smem_desc_sw128(al), smem_desc_sw128(bv), idesc, (hf | kk) != 0);
+                mma_tf32(oacc, smem_desc_sw128(a), smem_desc_sw128(bl), idesc, 1);
+                mma_tf32(oacc, smem_desc_sw128(a), smem_desc_sw128(bv), idesc, 1);
+            }
+            mma_commit(bar_o);
+        }
+        if (ok && !mbar_wait(bar_o, hf & 1, nullptr)) ok = false;
+        tc_fence_after();
+    }
+    red_sum[g * 128 + row] = sum;
+    __syncthreads();
+
+    // ---- 5. O row / sum: group g stores columns [16 g, 16 g + 16) -----------------
+    if (ok) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(lane_addr + 128 + g * 16, r);
+        tmem_ld_wait();
+        if (row < S) {
+            const float inv = 1.0f / (red_sum[row] + red_sum[128 + row]);
+            float *op = out + ((int64_t)b * S + row) * ((int64_t)heads * DH) + (int64_t)h * DH + g * 16;
+#pragma unroll
+            for (int d = 0; d < 16; d += 4)
+                *reinterpret_cast<float4 *>(op + d) =
+                    make_float4(__uint_as_float(r[d]) * inv, __uint_as_float(r[d + 1]) * inv,
+                                __uint_as_float(r[d + 2]) * inv, __uint_as_float(r[d + 3]) * inv);
+        }
+    } else if (t == 0) {
+        atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
+        mma_commit(bar_drain);
+        mbar_wait(bar_drain, 0, nullptr, 400000000ll);
+        mbar_wait(bar_ld, 0, nullptr, 400000000ll);  // no TMA copy may land after exit
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
 }  // namespace
 
 namespace lonnx {
+
+int make_tile_map_f32(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows);
 
 // Returns LONNX_E_UNSUPPORTED when the shape does not fit this kernel.
 int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld, const float *mask,
                  float *out, int B, int S, int heads, int dh, float scale) {
     if (dh != DH || S <= 0 || S > 128) return LONNX_E_UNSUPPORTED;
+    static const bool one_group = getenv("LONNX_ATTN_TC4") != nullptr;
+    auto al16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+    if (!one_group && (ld & 3) == 0 && al16(q) && al16(k) && al16(v) && (int64_t)B * S < ((int64_t)1 << 31)) {
+        CUtensorMap mq, mk, mv;
+        const int64_t rows = (int64_t)B * S, cols = (int64_t)heads * DH;
+        int rc = make_tile_map_f32(&mq, q, rows, cols, ld, 128);
+        if (!rc) rc = make_tile_map_f32(&mk, k, rows, cols, ld, 128);
+        if (!rc) rc = make_tile_map_f32(&mv, v, rows, cols, ld, 128);
+        if (rc) return rc;
+        static bool attr8_set[64] = {false};
+        if (!attr8_set[ctx->device & 63]) {
+            LONNX_CUDA(cudaFuncSetAttribute(k_attention_tc8, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM8));
+            attr8_set[ctx->device & 63] = true;
+        }
+        k_attention_tc8<<<B * heads, AT8, SMEM8, ctx->stream>>>(mq, mk, mv, mask, out, S, heads, scale,
+                                                                  ctx->dev_flags);
+        LONNX_CHECK_LAUNCH(ctx);
+        return LONNX_OK;
+    }
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {
         LONNX_CUDA(cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));

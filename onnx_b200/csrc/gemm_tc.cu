@@ -1012,6 +1012,12 @@ int pick_bn_conv(int M, bool res) {
 
 namespace lonnx {
 
+// 2-D fp32 tensor map (box = box_rows x 32, 128-byte swizzle) for other
+// tensor-core kernels of this library.
+int make_tile_map_f32(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+    return make_map(map, base, rows, cols, ld, box_rows);
+}
+
 int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, const float *bias, float *C, int M,
             int N, int K, int lda, int ldw, int ldc, float alpha, float beta, int epi, bool allow_scratch,
             bool split_k) {

@@ -338,6 +338,45 @@ def test_attention_direct(ctx):
     close(out.to_host(), ref, atol=1e-5, rtol=1e-5)
 
 
+@pytest.mark.parametrize("S,packed,masked", [(128, False, True), (77, True, True), (1, True, False),
+                                             (100, False, False), (33, True, True)])
+def test_attention_direct_shapes(ctx, S, packed, masked):
+    """The TMA-fed tensor-core attention at sequence lengths below 128 (the
+    128-row TMA box then reaches into the next sequence, or past the end of
+    the tensor for the last one), with Q/K/V packed in one [B, S, 3H] buffer
+    or in three [B, S, H] buffers, with and without the additive mask."""
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    rng = np.random.default_rng(S)
+    B, h, dh = 5, 12, 32
+    H = h * dh
+    qkv = rng.standard_normal((B, S, 3 * H)).astype(np.float32)
+    mask = np.zeros((B, 1, 1, S), np.float32)
+    if masked:
+        for bb in range(B):
+            mask[bb, ..., S - rng.integers(0, S):] = np.finfo(np.float32).min
+    q, k, v = qkv[..., :H], qkv[..., H:2 * H], qkv[..., 2 * H:]
+    split = lambda t, p: O.transpose(t.reshape(B, S, h, dh), p)
+    sc = O.matmul(split(q, [0, 2, 1, 3]), split(k, [0, 2, 3, 1]))
+    sc = O.binary("Div", sc, np.float32(np.sqrt(dh)))
+    if masked:
+        sc = O.binary("Add", sc, mask)
+    p = O.softmax(sc, -1)
+    ref = O.transpose(O.matmul(p, split(v, [0, 2, 1, 3])), [0, 2, 1, 3]).reshape(B, S, H)
+    out = DeviceTensor(ctx, (B, S, H), np.float32)
+    dm = DeviceTensor.from_host(ctx, mask) if masked else None
+    mp = dm.ptr if masked else None
+    if packed:
+        dq = DeviceTensor.from_host(ctx, qkv)
+        args = (dq.ptr, dq.ptr + 4 * H, dq.ptr + 8 * H, 3 * H)
+    else:
+        dq, dk, dv = (DeviceTensor.from_host(ctx, np.ascontiguousarray(a)) for a in (q, k, v))
+        args = (dq.ptr, dk.ptr, dv.ptr, H)
+    N.check(N.lib.lonnx_attention_f32(ctx.handle, *args, mp, out.ptr, B, S, h, dh, np.float32(np.sqrt(dh))))
+    ctx.sync()
+    close(out.to_host(), ref, atol=1e-5, rtol=1e-5)
+
+
 @pytest.mark.parametrize("xs,ws,stride,pad,relu", [((4, 64, 28, 28), (128, 64, 3, 3), 1, 1, 1),
                                                    ((2, 3, 64, 64), (64, 3, 7, 7), 2, 3, 1),
                                                    ((4, 256, 14, 14), (512, 256, 1, 1), 2, 0, 0),
