@@ -169,6 +169,21 @@ __global__ void k_split_pad_rows(const float *__restrict__ w, float *__restrict_
     }
 }
 
+// tap-major split: column tap * C + c of the output takes w[m][c * taps + tap]
+__global__ void k_split_rows_tapmajor(const float *__restrict__ w, float *__restrict__ hi, float *__restrict__ lo,
+                                      int M, int C, int taps) {
+    const int64_t K = (int64_t)C * taps, total = (int64_t)M * K;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += stride) {
+        const int64_t m = t / K;
+        const int k = (int)(t - m * K), tap = k / C, c = k - tap * C;
+        const float v = w[m * K + (int64_t)c * taps + tap];
+        const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+        hi[t] = h;
+        lo[t] = __fsub_rn(v, h);
+    }
+}
+
 // y = y + r (then ReLU): a Conv -> Add [-> Relu] chain off the tensor cores
 __global__ void k_add_relu(float *__restrict__ y, const float *__restrict__ r, int64_t n, int relu) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -376,9 +391,20 @@ int split_pad_rows(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int M, 
     return LONNX_OK;
 }
 
+int split_rows_tapmajor(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int M, int C, int taps) {
+    k_split_rows_tapmajor<<<grid_for(ctx, (int64_t)M * C * taps), 256, 0, ctx->stream>>>(w, hi, lo, M, C, taps);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+bool conv_nhwc_ok(int C, int kh, int kw) {
+    static const bool off = getenv("LONNX_CONV_NCHW_GATHER") != nullptr;
+    return !off && C % 32 == 0 && kh * kw > 1 && kh * kw <= 63;
+}
+
 int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, const float *wlo, const float *bias,
            const float *res, float *y, int N, int C, int H, int W, int M, int kh, int kw, int sh, int sw, int pt,
-           int pl, int pb, int pr, int dh, int dw, int group, int relu) {
+           int pl, int pb, int pr, int dh, int dw, int group, int relu, int w_tapmajor) {
     if (!x || !w || !y || N < 0 || C <= 0 || M <= 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 ||
         dh <= 0 || dw <= 0 || group <= 0 || C % group || M % group)
         return set_error(LONNX_E_BADARG, "conv2d: bad arguments");
@@ -396,24 +422,42 @@ int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, con
         // columns = output channels, contraction over (c, ky, kx) in the
         // reference's im2col order; input gathered inside the kernel, bias,
         // residual and ReLU in the epilogue, NCHW written directly
+        // NHWC gather: the input transposed once into scratch, the weights
+        // in tap-major column order (prepared that way, or split so here)
+        const bool nhwc = conv_nhwc_ok(C, kh, kw) && (int64_t)C * H * W < (1ll << 31);
         const int ldk = (K + 3) & ~3;
-        void *wt = nullptr;
-        if (!whi || !wlo) {
+        void *wt = nullptr, *xt = nullptr;
+        if (!whi || !wlo || (bool)w_tapmajor != nhwc) {
             int rc = ctx_alloc(ctx, (size_t)2 * M * ldk * 4, &wt);
             if (rc) return rc;
             whi = (const float *)wt;
             wlo = whi + (size_t)M * ldk;
-            rc = split_pad_rows(ctx, w, (float *)whi, (float *)wlo, M, K, ldk);
+            rc = nhwc ? split_rows_tapmajor(ctx, w, (float *)whi, (float *)wlo, M, C, kh * kw)
+                      : split_pad_rows(ctx, w, (float *)whi, (float *)wlo, M, K, ldk);
             if (rc) { ctx_free(ctx, wt); return rc; }
         }
+        if (nhwc) {
+            int rc = ctx_alloc(ctx, (size_t)N * C * H * W * 4, &xt);
+            if (!rc) {
+                const int64_t shp[4] = {N, C, H, W}, perm[4] = {0, 2, 3, 1};
+                rc = transpose_launch(ctx, x, 4, shp, 4, perm, xt);
+            }
+            if (rc) {
+                if (xt) ctx_free(ctx, xt);
+                if (wt) ctx_free(ctx, wt);
+                return rc;
+            }
+        }
         ConvArgs cv;
-        cv.x = x;
+        cv.x = nhwc ? (const float *)xt : x;
+        cv.nhwc = nhwc ? 1 : 0;
         cv.C = C; cv.H = H; cv.W = W; cv.kh = kh; cv.kw = kw; cv.sh = sh; cv.sw = sw;
         cv.pt = pt; cv.pl = pl; cv.dh = dh; cv.dw = dw; cv.Ho = Ho; cv.Wo = Wo;
         cv.img_rows = Ho * Wo;
         cv.res = res;
         int rc = conv_tc(ctx, cv, whi, wlo, ldk, bias, y, (int)P, M, K, relu ? LONNX_EPI_RELU : LONNX_EPI_NONE);
         if (wt) ctx_free(ctx, wt);
+        if (xt) ctx_free(ctx, xt);
         if (rc != LONNX_E_UNSUPPORTED) return rc;
     }
     k_conv2d_direct<<<grid_for(ctx, total), 256, 0, ctx->stream>>>(x, w, bias, y, N, C, H, W, M, kh, kw, sh, sw, pt,

@@ -329,7 +329,52 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 ++gj;
                 if (++gi == nk) { gi = 0; gt += (int)gridDim.x; }
             };
+            // NHWC path (cv.nhwc): stage i of a tile is tap (ky, kx) = the
+            // i / (C / 32)-th tap and channels [32 (i % (C / 32)), +32); each
+            // thread copies its NC channels as NC / 4 16-byte cp.async into
+            // chunk slots rotated by r (16-byte chunks, 8 per row)
+            int nt_tap = 0, nt_cb = 0, nt_ky = 0, nt_kx = 0, y0n = 0, x0n = 0;
+            auto gather_nhwc = [&]() {
+                if (gt != mt) {
+                    mt = gt;
+                    nt_tap = nt_cb = nt_ky = nt_kx = 0;
+                    const int p = tile_m0(gt) + r;
+                    vmask = 0;
+                    xr = cv.x;
+                    if (p < M) {
+                        const int hw = cv.Ho * cv.Wo, n = p / hw, rem = p - n * hw;
+                        const int oy = rem / cv.Wo, ox = rem - oy * cv.Wo;
+                        y0n = oy * cv.sh - cv.pt;
+                        x0n = ox * cv.sw - cv.pl;
+                        xr = cv.x + (int64_t)n * cv.C * HW;
+                        int ky = 0, kx = 0;
+                        for (int rr = 0; rr < khw; ++rr) {
+                            const int yy = y0n + ky * cv.dh, xx = x0n + kx * cv.dw;
+                            if ((unsigned)yy < (unsigned)cv.H && (unsigned)xx < (unsigned)cv.W) vmask |= 1ull << rr;
+                            if (++kx == cv.kw) { kx = 0; ++ky; }
+                        }
+                    }
+                }
+                const uint32_t row = smem_u32(stageA(gj % S)) + r * 128;
+                const bool in = (vmask >> nt_tap) & 1u;
+                const float *src = in ? xr + ((int64_t)(y0n + nt_ky * cv.dh) * cv.W + (x0n + nt_kx * cv.dw)) * cv.C +
+                                            nt_cb * BK + c0
+                                      : cv.x;
+#pragma unroll
+                for (int q4 = 0; q4 < NC / 4; ++q4) {
+                    const int qq = c0 / 4 + q4;
+                    cp_async16(row + (((qq + r) & 7) << 4), in ? src + q4 * 4 : cv.x, in ? 16u : 0u);
+                }
+                if (++nt_cb * BK == cv.C) {
+                    nt_cb = 0;
+                    ++nt_tap;
+                    if (++nt_kx == cv.kw) { nt_kx = 0; ++nt_ky; }
+                }
+                ++gj;
+                if (++gi == nk) { gi = 0; gt += (int)gridDim.x; }
+            };
             auto gather = [&](int j) {
+                if (cv.nhwc) { gather_nhwc(); return; }
                 if (cv.tab) { gather_tab(); return; }
                 const int t = step_tile(j), i = j % nk;
                 if (t != cur_tile) {
@@ -375,8 +420,19 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 cp_async_wait<D>();  // this thread's taps of step j have landed
                 const float *row = reinterpret_cast<const float *>(stageA(s) + r * 128);
                 float x[NC];
+                if (cv.nhwc) {
 #pragma unroll
-                for (int u = 0; u < NC; ++u) x[u] = row[(c0 + u + r) & 31];
+                    for (int q4 = 0; q4 < NC / 4; ++q4) {
+                        const float4 v4 = *reinterpret_cast<const float4 *>(row + (((c0 / 4 + q4 + r) & 7) << 2));
+                        x[q4 * 4] = v4.x;
+                        x[q4 * 4 + 1] = v4.y;
+                        x[q4 * 4 + 2] = v4.z;
+                        x[q4 * 4 + 3] = v4.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < NC; ++u) x[u] = row[(c0 + u + r) & 31];
+                }
                 if (!mbar_wait(afree(b), ((j / NAB) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
                 to_tmem(b, x);
@@ -1095,7 +1151,9 @@ int conv_tc(lonnx_ctx *ctx, const ConvArgs &cv, const float *Whi, const float *W
     const int tab_max = bn == 192 ? Cfg<192>::TAB_MAX
                         : bn == 64 ? (res ? Cfg<64, true>::TAB_MAX : Cfg<64>::TAB_MAX)
                                    : (res ? Cfg<128, true>::TAB_MAX : Cfg<128>::TAB_MAX);
-    a.tab = kend <= tab_max && cv.kh * cv.kw <= 63 && (int64_t)cv.C * cv.H * cv.W < (1ll << 24);
+    a.tab = !cv.nhwc && kend <= tab_max && cv.kh * cv.kw <= 63 && (int64_t)cv.C * cv.H * cv.W < (1ll << 24);
+    if (cv.nhwc && (cv.C % BK || cv.kh * cv.kw > 63 || K != cv.C * cv.kh * cv.kw))
+        return set_error(LONNX_E_UNSUPPORTED, "conv_tc: NHWC gather needs C % 32 == 0 and <= 63 taps");
     CUtensorMap mw, mwlo;
     int rc = make_map(&mw, Whi, M, K, ldw, bn);
     if (rc) return rc;

@@ -131,6 +131,7 @@ struct Step {
     std::shared_ptr<DevBuf> wlo;  // [N, K] low parts (wt + wlo == W^T exactly)
     std::shared_ptr<DevBuf> bias;
     int N = 0, K = 0, epi = 0;
+    int w_tapmajor = 0;  // conv: wt / wlo columns in (ky, kx, c) order (NHWC gather)
     std::vector<std::string> split_outputs;  // QKV: outputs per part (views), part width N/parts
     // LN
     std::string a, b;  // x (and residual) inputs
@@ -369,7 +370,8 @@ void exec_matmul(lonnx_graph *g, const NodeDef &n) {
 // input of a following Add (same shape as the Conv output; the caller
 // checks), whi/wlo = the weight split at prepare time.
 bool exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string *out_name = nullptr,
-               const Value *res = nullptr, const float *whi = nullptr, const float *wlo = nullptr) {
+               const Value *res = nullptr, const float *whi = nullptr, const float *wlo = nullptr,
+               int w_tapmajor = 0) {
     Value x = lookup(g, n.in.at(0)), w = lookup(g, n.in.at(1));
     Value bias;
     const bool has_bias = n.in.size() > 2 && !n.in[2].empty();
@@ -416,7 +418,7 @@ bool exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string
     ck(lonnx::conv2d(g->ctx, (const float *)x.dptr(), (const float *)w.dptr(), whi, wlo,
                      has_bias ? (const float *)bias.dptr() : nullptr, res ? (const float *)res->dptr() : nullptr,
                      (float *)y.dptr_mut(), N, C, H, W, M, kh, kw, (int)strides[0], (int)strides[1], pt, pl, pb, pr,
-                     (int)dil[0], (int)dil[1], group, relu));
+                     (int)dil[0], (int)dil[1], group, relu, w_tapmajor));
     g->env[out_name ? *out_name : n.out.at(0)] = y;
     return true;
 }
@@ -1206,7 +1208,7 @@ bool exec_conv_step(lonnx_graph *g, const Step &s) {
         ensure_dev(g, res);
     }
     const float *whi = s.wt ? (const float *)s.wt->p : nullptr, *wlo = s.wlo ? (const float *)s.wlo->p : nullptr;
-    return exec_conv(g, c, s.epi, &s.y, s.b.empty() ? nullptr : &res, whi, wlo);
+    return exec_conv(g, c, s.epi, &s.y, s.b.empty() ? nullptr : &res, whi, wlo, s.w_tapmajor);
 }
 
 void build_steps(lonnx_graph *g, bool fuse) {
@@ -1272,7 +1274,12 @@ void build_steps(lonnx_graph *g, bool fuse) {
         const int M = (int)W.shape[0], K = (int)(W.shape[1] * W.shape[2] * W.shape[3]), ldk = (K + 3) & ~3;
         st.wt = std::make_shared<DevBuf>(g->ctx, (size_t)M * ldk * 4);
         st.wlo = std::make_shared<DevBuf>(g->ctx, (size_t)M * ldk * 4);
-        ck(split_pad_rows(g->ctx, (const float *)W.dptr(), (float *)st.wt->p, (float *)st.wlo->p, M, K, ldk));
+        const int C = (int)W.shape[1], kh = (int)W.shape[2], kw = (int)W.shape[3];
+        st.w_tapmajor = conv_nhwc_ok(C, kh, kw) ? 1 : 0;
+        if (st.w_tapmajor)
+            ck(split_rows_tapmajor(g->ctx, (const float *)W.dptr(), (float *)st.wt->p, (float *)st.wlo->p, M, C, kh * kw));
+        else
+            ck(split_pad_rows(g->ctx, (const float *)W.dptr(), (float *)st.wt->p, (float *)st.wlo->p, M, K, ldk));
     }
     // QKV merge: three GEMM groups on one input feeding one attention group
     for (auto &at : groups) {

@@ -101,18 +101,26 @@ struct ConvArgs {
     int img_rows = 0;
     const float *res = nullptr;
     int tab = 0;  // set by conv_tc: the per-CTA tap table fits (see gemm_tc.cu)
+    int nhwc = 0; // x is NHWC and the weights are tap-major: K order (ky, kx, c)
 };
+// Convs gathered from an NHWC copy of their input (one tap's 32 consecutive
+// channels per K stage, 16-byte copies) with tap-major weights: C a multiple
+// of 32 and a kernel of 2..63 taps.
+bool conv_nhwc_ok(int C, int kh, int kw);
 // y[N, M, Ho, Wo] = conv(x, W) + bias (+ res) (ReLU if epi); W pre-split
 // into Whi, Wlo [M, ldw] (K = C*kh*kw columns used).  P = N*Ho*Wo.
 int conv_tc(lonnx_ctx *ctx, const ConvArgs &cv, const float *Whi, const float *Wlo, int ldw, const float *bias,
             float *y, int P, int M, int K, int epi);
 // weight [M, K] -> hi, lo [M, ldk] (tf32 split, zero padded)
 int split_pad_rows(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int M, int K, int ldk);
+// the same split with the columns reordered from (c, tap) to (tap, c):
+// hi[m][tap * C + c] = tf32(w[m][c * taps + tap]) (K = C * taps = ldk)
+int split_rows_tapmajor(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int M, int C, int taps);
 // Conv with optional pre-split weights (whi/wlo [M, ldk], ldk = (K+3)&~3, or
 // nullptr) and an optional residual added before the ReLU.
 int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, const float *wlo, const float *bias,
            const float *res, float *y, int N, int C, int H, int W, int M, int kh, int kw, int sh, int sw, int pt,
-           int pl, int pb, int pr, int dh, int dw, int group, int relu);
+           int pl, int pb, int pr, int dh, int dw, int group, int relu, int w_tapmajor = 0);
 // Fused attention on tensor cores (dh = 32, S <= 128); LONNX_E_UNSUPPORTED otherwise.
 int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld, const float *mask,
                  float *out, int B, int S, int heads, int dh, float scale);

@@ -408,14 +408,18 @@ def test_conv_tensor_core_path_vs_oracle(ctx, xs, ws, stride, pad, relu):
     close(y.to_host(), ref)
 
 
-@pytest.mark.parametrize("dil,pads", [((2, 2), (2, 2, 2, 2)), ((1, 3), (1, 0, 2, 3))])
-def test_conv_tensor_core_dilation_asymmetric_pads(ctx, dil, pads):
-    """Dilated taps and asymmetric pads through the implicit-GEMM gather,
-    against a float64 direct convolution (tolerance of the 3xTF32 GEMM)."""
+@pytest.mark.parametrize("dil,pads,c,k", [((2, 2), (2, 2, 2, 2), 40, 3), ((1, 3), (1, 0, 2, 3), 40, 3),
+                                          ((2, 2), (2, 2, 2, 2), 64, 3), ((1, 3), (1, 0, 2, 3), 32, 5),
+                                          ((1, 1), (0, 0, 0, 0), 96, 2)])
+def test_conv_tensor_core_dilation_asymmetric_pads(ctx, dil, pads, c, k):
+    """Dilated taps and asymmetric pads through the implicit-GEMM gather
+    (from NCHW for C = 40; from the NHWC copy, tap-major weights, for C a
+    multiple of 32), against a float64 direct convolution (tolerance of the
+    3xTF32 GEMM)."""
     from onnx_b200 import _native as N
     from onnx_b200.tensor import DeviceTensor
     rng = np.random.default_rng(11)
-    n, c, h, w, m, k = 3, 40, 23, 21, 96, 3
+    n, h, w, m = 3, 23, 21, 96
     x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
     wt = (rng.standard_normal((m, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32)
     pt, pl, pb, pr = pads
