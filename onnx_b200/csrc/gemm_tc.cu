@@ -15,9 +15,9 @@
 // CTA = 20 warps, one 128 x BN output tile (BN = 128 or 192):
 //   warp 0      TMA producer (one lane): A, W_hi, W_lo tiles of 32 K-columns
 //               (128 bytes = one 128B-swizzle row) per stage, 3-4 stages
-//   warp 1      TMEM allocator + MMA issuer (one lane): 4 K-steps x 3
-//               products per stage, A from TMEM, W from shared memory, into
-//               one of two TMEM chunk accumulators
+//   warps 1, 2  MMA issuers (one lane each, even / odd stages; warp 1 also
+//               owns TMEM): 4 K-steps x 3 products per stage, A from TMEM, W
+//               from shared memory, into one of two TMEM chunk accumulators
 //   warps 4-7   move each stage's A rows into TMEM as tf32 hi and lo parts
 //   warps 8-19  drain each chunk accumulator into fp32 registers (round to
 //               nearest), 64 columns per warp, then run the epilogue
@@ -43,8 +43,8 @@ constexpr int BM = 128;
 constexpr int BK = 32;                  // fp32 elements per 128-byte row
 constexpr int A_TILE = BM * BK * 4;     // 16 KB
 constexpr int kThreads = 640;           // 20 warps
-// warp roles: 0 TMA, 1 MMA + TMEM owner, 4-7 A -> TMEM, 8-19 accumulate/epilogue
-constexpr int W_TMA = 0, W_MMA = 1, W_A0 = 4, W_ACC0 = 8;
+// warp roles: 0 TMA, 1-2 MMA (1 owns TMEM), 4-7 A -> TMEM, 8-19 accumulate/epilogue
+constexpr int W_TMA = 0, W_MMA = 1, W_MMA2 = 2, W_A0 = 4, W_ACC0 = 8;
 // kernel modes: plain GEMM (A by TMA, row-major C, one tile per CTA);
 // implicit conv (A gathered, NCHW C, persistent); implicit conv + residual
 constexpr int MODE_GEMM = 0, MODE_CONV = 1, MODE_CONV_RES = 2;
@@ -172,7 +172,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             mbar_init(tdrain(b), NACC);
         }
         for (int b = 0; b < NAB; ++b) mbar_init(afree(b), 1);
-        mbar_init(drainbar, 1);
+        mbar_init(drainbar, 2);  // one commit per issuing thread
         *abort_flag = 0;
         fence_mbar_init();
         if constexpr (!CONV) prefetch_tmap(&tmA);
@@ -227,10 +227,18 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 }
             }
         }
-    } else if (warp == W_MMA) {
+    } else if (warp == W_MMA || warp == W_MMA2) {
+        // two issuing threads, even and odd stages: issuing one tcgen05.mma
+        // costs its thread ~80-100 SM cycles, more than a 128 x 128 x 8 tf32
+        // MMA takes to run, so one thread could not keep the tensor pipe fed
+        // (measured: 12 MMAs per stage issued in ~1.6k cycles against ~0.8k
+        // of execution).  Stage j uses accumulator chunk j & 1, so each
+        // issuer owns one chunk; ring slots and TMEM A buffers are per stage.
+        // No barrier can run two phases ahead of an issuer: the A warps and
+        // the TMA stay within NAB <= S stages of the oldest unfinished MMA.
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(BM, BN);
-            for (int j = 0; j < total && ok; ++j) {
+            for (int j = warp - W_MMA; j < total && ok; j += 2) {
                 const int s = j % S, b = j & 1;
                 if (!mbar_wait(conv(s), (j / S) & 1, abort_flag)) { ok = false; break; }
                 // implicit conv: the A warps do not wait for the W tiles, so the MMA does
@@ -624,7 +632,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     if (*abort_flag) {
         // drain before releasing TMEM / exiting: MMAs already issued, and TMA
         // loads that may still land in this CTA's shared memory (bounded waits)
-        if (warp == W_MMA && lane == 0) {
+        if ((warp == W_MMA || warp == W_MMA2) && lane == 0) {
             mma_commit(drainbar);
             mbar_wait(drainbar, 0, nullptr, 400000000ll);
         }
