@@ -65,6 +65,10 @@ struct Cfg {
     static constexpr int TAB_MAX = (SMEM - 1024 - TAB_OFF) / 4;  // tap-table entries
     static constexpr int GROUPS = BN / 64;              // accumulator column groups of 64
     static constexpr int NACC = 4 * GROUPS;             // accumulator warps 8 .. 8 + NACC - 1
+    // GEMM epilogue: one 32 x 16 staging block per accumulator warp at TAB_OFF
+    // (16-byte rows of 20 floats: conflict-free float4 writes)
+    static constexpr int STG_PITCH = 20;
+    static constexpr int GEMM_SMEM = TAB_OFF + NACC * 32 * STG_PITCH * 4 + 1024;
     // A warpgroups: warps 4-7, plus warps 8 + NACC .. +3 when the
     // accumulators leave four warps idle (BN <= 128); each group then moves
     // 16 of a stage's 32 K-columns
@@ -75,6 +79,7 @@ struct Cfg {
     static constexpr int NAB = 2 * BN + 3 * 64 <= 512 ? 3 : 2;
     static constexpr int TMEM_COLS = 2 * BN + NAB * 64 <= 256 ? 256 : 512;
     static_assert(3 * STAGES + 5 + NAB <= 30, "barrier area");
+    static_assert(RES || GEMM_SMEM <= SMEM, "GEMM epilogue staging must fit beside the ring");
 };
 
 
@@ -137,13 +142,15 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     // GEMM split-K: CTA b takes tile b / ksplit and that tile's K stages
     // [ks * chunk, ks * chunk + nk); its raw sums go to C + ks * split_stride
     const int ks = CONV ? 0 : (int)blockIdx.x % ksplit;
-    const int t0 = CONV ? (int)blockIdx.x : (int)blockIdx.x / ksplit;
+    const int t0 = CONV || ksplit == 1 ? (int)blockIdx.x : (int)blockIdx.x / ksplit;
     const int chunk = (nk_all + ksplit - 1) / ksplit;
     const int nk = CONV ? nk_all : min(chunk, nk_all - ks * chunk);
     const int kofs = ks * chunk * BK;
     if (!CONV && ksplit > 1) C += ks * split_stride;
-    const int my_tiles = CONV ? ((int)blockIdx.x < ntiles ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0)
-                              : (t0 < ntiles && nk > 0 ? 1 : 0);
+    // persistent (CTA b takes tiles b, b + gridDim.x, ...) except for split-K
+    const int my_tiles = CONV || ksplit == 1
+                             ? ((int)blockIdx.x < ntiles && nk > 0 ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0)
+                             : (t0 < ntiles && nk > 0 ? 1 : 0);
     const int total = my_tiles * nk;  // (tile, stage) steps of this CTA
     auto tile_n0 = [&](int t) { return (t % ntn) * BN; };
     auto tile_m0 = [&](int t) { return (t / ntn) * BM; };
@@ -571,53 +578,58 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 }
                 continue;
             }
-            // row-major epilogue (one tile per CTA, the ring is idle now):
-            // raw sums staged row-major in the stage buffers, then one pass
-            // that applies alpha, bias and the activation and writes
-            // coalesced 16-byte stores.  The activation code appears once (a
-            // per-element unrolled epilogue with Erf-GELU inlined overflows
-            // the instruction cache).
-            constexpr int PITCH = BN + 4;  // floats; keeps the per-row writes conflict-free
-            static_assert(BM * PITCH * 4 + BN * 4 <= G::STAGES * G::STAGE, "C tile + bias must fit in the stage ring");
-            float *ctile = reinterpret_cast<float *>(smem);
-            float *sbias = ctile + BM * PITCH;
-            const int tid = threadIdx.x - W_ACC0 * 32;
-            for (int c = tid; c < BN; c += NACC * 32) {
+            // row-major epilogue, overlapping the next tile's loads and MMAs:
+            // each warp moves its 32 rows x 64 columns out 16 columns at a
+            // time through a private 32 x 16 staging block in shared memory
+            // (the tail past the ring), so that its stores coalesce along
+            // rows; alpha, bias and the activation are applied in a
+            // non-unrolled loop (the activation code appears once per value
+            // of a float4: an unrolled per-element epilogue with Erf-GELU
+            // inlined overflows the instruction cache).
+            float *sb = ebias + (tt & 1) * BN;
+            for (int c = threadIdx.x - W_ACC0 * 32; c < BN; c += NACC * 32) {
                 const int col = n0 + c;
                 float bv = 0.0f;
                 if (bias && col < N) bv = beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col));
-                sbias[c] = bv;
+                sb[c] = bv;
             }
-#pragma unroll
-            for (int j = 0; j < 64; j += 4)
-                *reinterpret_cast<float4 *>(ctile + rloc * PITCH + grp * 64 + j) =
-                    make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
             asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
-            constexpr int V4 = BN / 4;  // float4 per tile row
-            const bool vec = (ldc & 3) == 0 && n0 + BN <= N;
-#pragma unroll 1
-            for (int e = tid; e < BM * V4; e += NACC * 32) {
-                const int rr = e / V4, c4 = e % V4;
-                const int grow = m0 + rr;
-                if (grow >= M) continue;
-                const float4 raw = *reinterpret_cast<const float4 *>(ctile + rr * PITCH + c4 * 4);
-                float v[4] = {raw.x, raw.y, raw.z, raw.w};
-                const int col0 = n0 + c4 * 4;
+            float *stg = reinterpret_cast<float *>(smem + G::TAB_OFF) + (warp - W_ACC0) * (32 * G::STG_PITCH);
+            const int rbase = m0 + q * 32, cbase = n0 + grp * 64;
+            const float *sbg = sb + grp * 64;
+            const bool vec = (ldc & 3) == 0 && (N & 3) == 0 && ((uintptr_t)C & 15) == 0;
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    float x = v[u];
-                    if (alpha != 1.0f) x = __fmul_rn(x, alpha);
-                    if (bias) x = __fadd_rn(x, sbias[c4 * 4 + u]);
-                    if (epi == LONNX_EPI_RELU) x = x > 0.0f ? x : 0.0f;
-                    else if (epi == LONNX_EPI_GELU_ERF) x = lonnx_gelu_chain(x);
-                    v[u] = x;
-                }
-                float *dst = C + (int64_t)grow * ldc + col0;
-                if (vec) {
-                    *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-                } else {
-                    for (int u = 0; u < 4; ++u)
-                        if (col0 + u < N) dst[u] = v[u];
+            for (int ch = 0; ch < 4; ++ch) {
+                __syncwarp();
+#pragma unroll
+                for (int u = 0; u < 16; u += 4)
+                    *reinterpret_cast<float4 *>(stg + lane * G::STG_PITCH + u) =
+                        make_float4(acc[ch * 16 + u], acc[ch * 16 + u + 1], acc[ch * 16 + u + 2], acc[ch * 16 + u + 3]);
+                __syncwarp();
+                // float4 e4 = lane + 32 i of the 32 x 16 block: row e4 / 4, columns 4 (e4 % 4) ..
+#pragma unroll 1
+                for (int i = 0; i < 4; ++i) {
+                    const int e4 = lane + 32 * i, rr = e4 >> 2, c4 = (e4 & 3) * 4;
+                    const int grow = rbase + rr, col0 = cbase + ch * 16 + c4;
+                    const float4 raw = *reinterpret_cast<const float4 *>(stg + rr * G::STG_PITCH + c4);
+                    float v[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        float x = v[u];
+                        if (alpha != 1.0f) x = __fmul_rn(x, alpha);
+                        if (bias) x = __fadd_rn(x, sbg[ch * 16 + c4 + u]);
+                        if (epi == LONNX_EPI_RELU) x = x > 0.0f ? x : 0.0f;
+                        else if (epi == LONNX_EPI_GELU_ERF) x = lonnx_gelu_fast(x);
+                        v[u] = x;
+                    }
+                    if (grow >= M) continue;
+                    float *dst = C + (int64_t)grow * ldc + col0;
+                    if (vec && col0 + 3 < N) {
+                        *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+                    } else {
+                        for (int u = 0; u < 4; ++u)
+                            if (col0 + u < N) dst[u] = v[u];
+                    }
                 }
             }
         }
@@ -988,10 +1000,10 @@ int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, cons
     }
     const int64_t tiles = (int64_t)((N + BN - 1) / BN) * ((M + BM - 1) / BM);
     if (tiles >= (1ll << 31)) return lonnx::set_error(LONNX_E_UNSUPPORTED, "gemm_tc: too many tiles");
-    // the NCHW (conv) epilogue needs no shared memory: one persistent CTA per SM
-    const int64_t grid = MODE != MODE_GEMM ? (tiles > ctx->num_sms ? ctx->num_sms : tiles) : tiles * ksplit;
-    // the tap table (the tail of shared memory) exists only for the implicit conv
-    const int smem = MODE != MODE_GEMM ? G::SMEM : G::TAB_OFF + 1024;
+    // one persistent CTA per SM (split-K: one CTA per tile and split)
+    const int64_t grid = ksplit == 1 ? (tiles > ctx->num_sms ? ctx->num_sms : tiles) : tiles * ksplit;
+    // the tail of shared memory holds the conv tap table or the GEMM epilogue staging
+    const int smem = MODE != MODE_GEMM ? G::SMEM : G::GEMM_SMEM;
     k_gemm_tf32x3<BN, MODE><<<(unsigned)grid, kThreads, smem, ctx->stream>>>(ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi,
                                                                 ctx->dev_flags, cv, ksplit, split_stride);
     LONNX_CHECK_LAUNCH(ctx);

@@ -173,3 +173,21 @@ __device__ __forceinline__ float lonnx_gelu_chain(float x) {
     const float c = __fadd_rn(e, 1.0f);
     return __fmul_rn(__fmul_rn(x, c), 0.5f);
 }
+
+// The same GELU (A&S 7.1.26 erf of x / sqrt 2) for the fused GEMM epilogue,
+// where it costs ~15 instructions instead of ~55: x times RN(1/sqrt 2)
+// instead of the division, an approximate reciprocal for t, the polynomial
+// in FMAs and __expf.  Each step is within a few ulp of the chain above, so
+// the result is well inside the GEMM's own tolerance (|err| <= 1e-4 +
+// 1e-4 |ref|); inf and NaN behave as in the chain.
+__device__ __forceinline__ float lonnx_gelu_fast(float x) {
+    const float a1 = 0.254829592f, a2 = -0.284496736f, a3 = 1.421413741f;
+    const float a4 = -1.453152027f, a5 = 1.061405429f, p = 0.3275911f;
+    const float a = x * 0.707106769084930419921875f;
+    const float ax = fabsf(a);
+    const float t = __fdividef(1.0f, fmaf(p, ax, 1.0f));
+    const float poly = fmaf(fmaf(fmaf(fmaf(a5, t, a4), t, a3), t, a2), t, a1);
+    const float y = fmaf(-poly * t, __expf(-ax * ax), 1.0f);
+    const float erf = copysignf(y, a);
+    return x * fmaf(0.5f, erf, 0.5f);
+}
