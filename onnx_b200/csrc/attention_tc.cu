@@ -239,11 +239,24 @@ k_attention_tc(const float *__restrict__ q, const float *__restrict__ k, const f
 //      [64 g, 64 g + 64) for the row max and, in each 64-key half, the 32
 //      keys [64 hf + 32 g, +32) for e = exp(..) -> E; the partial maxima and
 //      sums meet in shared memory;
-//   4. O += E V per half as before; 5. each group stores 16 of the 32 columns.
+//   4. O += E V per half, the three 3xTF32 products issued by three threads
+//      into three accumulators; 5. each group sums the three and stores 16 of
+//      the 32 columns.
 // The TMA loads replace 24 dependent 16-byte global loads per thread, which
 // were the kernel's main stall, and the second warp group halves each
-// thread's softmax work.
+// thread's softmax work.  The scores are exponentiated as 2^(u - u_max),
+// u = s log2(e) / scale + mask log2(e): one FMA and one ex2.approx per score
+// instead of expf's range reduction (the softmax changes by ~1e-6 relative,
+// inside the 3xTF32 products' own error).
 constexpr int AT8 = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+// 2^x by the hardware's approximate base-2 exponential (max relative error
+// ~2^-22; 2^-inf = 0)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 constexpr int OFF_RED = OFF_MASK + 128 * 4;          // [2][128] max, [2][128] sum
 constexpr int OFF_BAR8 = OFF_RED + 4 * 128 * 4;
 constexpr int SMEM8 = OFF_BAR8 + 64 + 1024;
@@ -267,8 +280,8 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     if (t == 0) {
         mbar_init(bar_ld, 1);
         mbar_init(bar_s, 1);
-        mbar_init(bar_o, 1);
-        mbar_init(bar_drain, 1);
+        mbar_init(bar_o, 3);  // one commit per P.V product issuer
+        mbar_init(bar_drain, 3);
         fence_mbar_init();
         prefetch_tmap(&tq);
         prefetch_tmap(&tk);
@@ -282,7 +295,9 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         tmem_alloc(smem_u32(tmem_slot), 256);
         tmem_relinquish();
     }
-    if (t < 128) msk[t] = (maskadd && t < S) ? maskadd[(int64_t)b * S + t] : 0.0f;
+    // the mask in log2 units (scores are exponentiated as 2^(u - u_max) with
+    // u = s * log2(e) / scale + mask * log2(e))
+    if (t < 128) msk[t] = (maskadd && t < S) ? maskadd[(int64_t)b * S + t] * kLog2e : 0.0f;
     __syncthreads();  // barrier inits visible before anyone waits on them
     bool ok = mbar_wait(bar_ld, 0, nullptr);
 
@@ -343,8 +358,8 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     // ---- 3. softmax: two warps per TMEM lane quarter, keys split -------------------
     const int g = warp >> 2, row = (warp & 3) * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const float inv_scale = 1.0f / scale;
-    float mx = 0.0f;
+    const float c2 = kLog2e / scale;
+    float mx = 0.0f;  // the reference's running max starts at 0; 0 maps to 0 in log2 units
     if (ok) {
 #pragma unroll
         for (int c = 2 * g; c < 2 * g + 2; ++c) {
@@ -354,7 +369,7 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
                 const int key = c * 32 + j;
-                if (key < S) mx = fmaxf(mx, __uint_as_float(r[j]) * inv_scale + msk[key]);
+                if (key < S) mx = fmaxf(mx, fmaf(__uint_as_float(r[j]), c2, msk[key]));
             }
         }
     }
@@ -374,7 +389,7 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int key = c * 32 + ch * 4 + u;
-                    e[u] = key < S ? expf(__uint_as_float(r[ch * 4 + u]) * inv_scale + msk[key] - mx) : 0.0f;
+                    e[u] = key < S ? ex2_approx(fmaf(__uint_as_float(r[ch * 4 + u]), c2, msk[key]) - mx) : 0.0f;
                     sum += e[u];
                 }
                 const float4 ev = make_float4(e[0], e[1], e[2], e[3]);
@@ -386,18 +401,21 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
-        if (t == 0 && ok) {
+        // the three 3xTF32 products of E.V are issued by three threads
+        // (lanes 0 of warps 0-2) into three accumulators O_p = TMEM columns
+        // [128 + 32 p, +32): one thread issuing all 24 small MMAs was the
+        // phase's bottleneck; the epilogue adds the three
+        if ((t & 31) == 0 && warp < 3 && ok) {
             constexpr uint32_t idesc = idesc_tf32(128, DH);
-            const uint32_t oacc = tmem + 128;
+            const uint32_t oacc = tmem + 128 + warp * 32;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
                 const uint32_t atom = kk >> 2, ko = (kk & 3) * 32, vatom = hf * 2 + atom;
-                const uint32_t a = smem_u32(sm + OFF_E + atom * TILE) + ko, al = smem_u32(sm + OFF_ELO + atom * TILE) + ko;
-                const uint32_t bv = smem_u32(sm + OFF_VT + vatom * 32 * ROWB) + ko;
-                const uint32_t bl = smem_u32(sm + OFF_VTLO + vatom * 32 * ROWB) + ko;
-                mma_tf32(oacc, smem_desc_sw128(al), smem_desc_sw128(bv), idesc, (hf | kk) != 0);
-                mma_tf32(oacc, smem_desc_sw128(a), smem_desc_sw128(bl), idesc, 1);
-                mma_tf32(oacc, smem_desc_sw128(a), smem_desc_sw128(bv), idesc, 1);
+                const uint32_t a = warp == 0 ? smem_u32(sm + OFF_ELO + atom * TILE) + ko
+                                             : smem_u32(sm + OFF_E + atom * TILE) + ko;
+                const uint32_t bv = warp == 1 ? smem_u32(sm + OFF_VTLO + vatom * 32 * ROWB) + ko
+                                              : smem_u32(sm + OFF_VT + vatom * 32 * ROWB) + ko;
+                mma_tf32(oacc, smem_desc_sw128(a), smem_desc_sw128(bv), idesc, (hf | kk) != 0);
             }
             mma_commit(bar_o);
         }
@@ -409,9 +427,15 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
 
     // ---- 5. O row / sum: group g stores columns [16 g, 16 g + 16) -----------------
     if (ok) {
-        uint32_t r[16];
+        uint32_t r[16], r1[16], r2[16];
         tmem_ld_32x32b_x16(lane_addr + 128 + g * 16, r);
+        tmem_ld_32x32b_x16(lane_addr + 160 + g * 16, r1);
+        tmem_ld_32x32b_x16(lane_addr + 192 + g * 16, r2);
         tmem_ld_wait();
+#pragma unroll
+        for (int d = 0; d < 16; ++d)
+            r[d] = __float_as_uint(__fadd_rn(__fadd_rn(__uint_as_float(r[d]), __uint_as_float(r1[d])),
+                                             __uint_as_float(r2[d])));
         if (row < S) {
             const float inv = 1.0f / (red_sum[row] + red_sum[128 + row]);
             float *op = out + ((int64_t)b * S + row) * ((int64_t)heads * DH) + (int64_t)h * DH + g * 16;
@@ -421,8 +445,9 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
                     make_float4(__uint_as_float(r[d]) * inv, __uint_as_float(r[d + 1]) * inv,
                                 __uint_as_float(r[d + 2]) * inv, __uint_as_float(r[d + 3]) * inv);
         }
-    } else if (t == 0) {
-        atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
+    } else if ((t & 31) == 0 && warp < 3) {
+        // every thread that issued MMAs drains its own before TMEM is freed
+        if (t == 0) atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
         mma_commit(bar_drain);
         mbar_wait(bar_drain, 0, nullptr, 400000000ll);
         mbar_wait(bar_ld, 0, nullptr, 400000000ll);  // no TMA copy may land after exit
