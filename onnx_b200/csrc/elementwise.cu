@@ -133,7 +133,9 @@ __device__ __forceinline__ float unop(float x) {
     if (OP == LONNX_SQRT) return __fsqrt_rn(x);
     if (OP == LONNX_ERF) return lonnx_erf_as(x);
     if (OP == LONNX_EXP) return expf(x);
-    return lonnx_gelu_chain(x);
+    // the fused GELU op (no single reference node): the fast evaluation of
+    // the same A&S formula, within a few ulp of the exported node chain
+    return lonnx_gelu_fast(x);
 }
 
 template <int OP>

@@ -239,21 +239,44 @@ __global__ void k_maxpool2d(const float *__restrict__ x, float *__restrict__ y, 
     const int r0 = oy * sh - pt, c0 = ox * sw - pl;
     const int rmin = max(r0, 0), rmax = min(r0 + kh, H);
     const int cmin = max(c0, 0), cmax = min(c0 + kw, W);
+    if (KH > 0) {
+        // two planes per iteration: 2 * KH * KW independent loads in flight
+        constexpr int T = KH * KW > 0 ? KH * KW : 1;
+        int off[T];
+        bool ok[T];
+#pragma unroll
+        for (int i = 0; i < KH; ++i)
+#pragma unroll
+            for (int j = 0; j < KW; ++j) {
+                const int r = r0 + i, c = c0 + j;
+                ok[i * KW + j] = r >= 0 && r < H && c >= 0 && c < W;
+                off[i * KW + j] = r * W + c;
+            }
+        const int64_t step = (int64_t)gridDim.y;
+        for (int64_t nc = blockIdx.y; nc < planes; nc += 2 * step) {
+            const bool two = nc + step < planes;
+            const float *xa = x + nc * H * W, *xb = x + (two ? nc + step : nc) * H * W;
+            float va[T], vb[T];
+#pragma unroll
+            for (int i = 0; i < T; ++i) {
+                va[i] = ok[i] ? __ldg(xa + off[i]) : -INFINITY;
+                vb[i] = ok[i] ? __ldg(xb + off[i]) : -INFINITY;
+            }
+            float ma = -INFINITY, mb = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < T; ++i) {
+                ma = fmaxf(ma, va[i]);
+                mb = fmaxf(mb, vb[i]);
+            }
+            y[nc * per_plane + t] = ma;
+            if (two) y[(nc + step) * per_plane + t] = mb;
+        }
+        return;
+    }
     for (int64_t nc = blockIdx.y; nc < planes; nc += gridDim.y) {
         const float *xp = x + nc * H * W;
         float m = -INFINITY;
-        if (KH > 0) {
-            float v[KH * KW > 0 ? KH * KW : 1];
-#pragma unroll
-            for (int i = 0; i < KH; ++i)
-#pragma unroll
-                for (int j = 0; j < KW; ++j) {
-                    const int r = r0 + i, c = c0 + j;
-                    v[i * KW + j] = (r >= 0 && r < H && c >= 0 && c < W) ? __ldg(xp + r * W + c) : -INFINITY;
-                }
-#pragma unroll
-            for (int i = 0; i < KH * KW; ++i) m = fmaxf(m, v[i]);
-        } else {
+        {
             for (int r = rmin; r < rmax; ++r)
                 for (int c = cmin; c < cmax; ++c) m = fmaxf(m, __ldg(xp + r * W + c));
         }
