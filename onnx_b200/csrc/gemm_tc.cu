@@ -1060,15 +1060,20 @@ bool pair_enabled() {
 
 // Tile width for N: 192 or 128, whichever divides N, else the one with the
 // least padding.
-int pick_bn(int N) {
+int pick_bn(int M, int N, int sms) {
     static const int forced = [] {
         const char *e = getenv("LONNX_GEMM_BN");
         return e ? atoi(e) : 0;
     }();
     if (forced == 128 || forced == 192) return forced;
-    if (N % 192 == 0) return 192;
-    if (N % 128 == 0) return 128;
-    return ((N + 191) / 192 * 192 - N) < ((N + 127) / 128 * 128 - N) ? 192 : 128;
+    int bn;
+    if (N % 192 == 0) bn = 192;
+    else if (N % 128 == 0) bn = 128;
+    else bn = ((N + 191) / 192 * 192 - N) < ((N + 127) / 128 * 128 - N) ? 192 : 128;
+    // fewer 192-wide tiles than SMs: 128-wide tiles spread the work over
+    // more SMs (each output element is summed in the same order either way)
+    if (bn == 192 && (int64_t)((M + BM - 1) / BM) * ((N + 191) / 192) < sms) bn = 128;
+    return bn;
 }
 
 // Conv tile width: the least padding of M among 128, 192 and 64 (ties to
@@ -1101,7 +1106,7 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
     if (!Wlo) return set_error(LONNX_E_UNSUPPORTED, "gemm_tc: weight must be pre-split");
     if (M <= 0 || N <= 0 || K <= 0 || (lda & 3) || (ldw & 3) || !al16(A) || !al16(Whi) || !al16(Wlo))
         return set_error(LONNX_E_UNSUPPORTED, "gemm_tc: operands not 16-byte aligned");
-    const int bn = pick_bn(N);
+    const int bn = pick_bn(M, N, ctx->num_sms);
     CUtensorMap ma, mw, mwlo;
     int rc = make_map(&ma, A, M, K, lda, BM);
     if (rc) return rc;
