@@ -118,6 +118,37 @@ __global__ void k_gemm_rowdot(const float *__restrict__ A, const float *__restri
     }
 }
 
+// The same sums for one small product (batch 1, A and B fit in 48 KB of
+// shared memory): one block stages A [M, K] and B with coalesced loads, then
+// each thread sums its output in the same order from shared memory.  The
+// per-thread version waits on global loads inside its sequential sum.
+template <bool TB>
+__global__ void __launch_bounds__(256) k_gemm_rowdot_smem(const float *__restrict__ A, const float *__restrict__ B,
+                                                          const float *__restrict__ bias, const float *__restrict__ res,
+                                                          float *__restrict__ C, int M, int N, int K, float alpha,
+                                                          float beta, int epi) {
+    extern __shared__ float sh[];
+    float *as = sh, *bs = sh + (int64_t)M * K;
+    const int na = M * K, nb = K * N;
+    for (int i = threadIdx.x; i < na; i += blockDim.x) as[i] = __ldg(A + i);
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) bs[i] = __ldg(B + i);
+    __syncthreads();
+    for (int t = threadIdx.x; t < M * N; t += blockDim.x) {
+        const int m = t / N, n = t - m * N;
+        const float *a = as + m * K;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int k = 0; k < K; ++k) acc = __fadd_rn(acc, __fmul_rn(a[k], TB ? bs[n * K + k] : bs[k * N + n]));
+        float v = acc;
+        if (alpha != 1.0f) v = __fmul_rn(v, alpha);
+        if (bias) v = __fadd_rn(v, beta == 1.0f ? bias[n] : __fmul_rn(beta, bias[n]));
+        if (res) v = __fadd_rn(v, res[t]);
+        if (epi == LONNX_EPI_RELU) v = v > 0.0f ? v : 0.0f;
+        else if (epi == LONNX_EPI_GELU_ERF) v = lonnx_gelu_chain(v);
+        C[t] = v;
+    }
+}
+
 // Direct NCHW convolution, one thread per output element, summing over
 // (c, ky, kx) in the im2col row order of MathOps.Conv2D with a separate
 // multiply and add (MathOps.cs:821-846), then the bias pass (:862-872) and
@@ -214,6 +245,15 @@ int transpose_launch(lonnx_ctx *ctx, const void *x, int elem_bytes, const int64_
 int gemm_simt(lonnx_ctx *ctx, const float *A, const float *B, const float *bias, float *C,
               int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
               float alpha, float beta, int epi, const float *residual) {
+    if (batch == 1 && (int64_t)M * N <= 256 && ((int64_t)M * K + (int64_t)K * N) * 4 <= 48 * 1024) {
+        const size_t smem = ((size_t)M * K + (size_t)K * N) * 4;
+        if (transB)
+            k_gemm_rowdot_smem<true><<<1, 256, smem, ctx->stream>>>(A, B, bias, residual, C, M, N, K, alpha, beta, epi);
+        else
+            k_gemm_rowdot_smem<false><<<1, 256, smem, ctx->stream>>>(A, B, bias, residual, C, M, N, K, alpha, beta, epi);
+        LONNX_CHECK_LAUNCH(ctx);
+        return LONNX_OK;
+    }
     if ((int64_t)batch * M * N <= 16384) {
         const int64_t total = (int64_t)batch * M * N;
         const int blocks = (int)((total + 127) / 128);

@@ -371,11 +371,14 @@ void exec_matmul(lonnx_graph *g, const NodeDef &n) {
 // checks), whi/wlo = the weight split at prepare time.
 bool exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string *out_name = nullptr,
                const Value *res = nullptr, const float *whi = nullptr, const float *wlo = nullptr,
-               int w_tapmajor = 0) {
+               int w_tapmajor = 0, const Value *bias_add = nullptr) {
     Value x = lookup(g, n.in.at(0)), w = lookup(g, n.in.at(1));
     Value bias;
-    const bool has_bias = n.in.size() > 2 && !n.in[2].empty();
-    if (has_bias) bias = lookup(g, n.in[2]);
+    // bias_add: a following per-channel Add folded in as the bias (the conv
+    // has none); the bias pass after the sum is the Add node's one rounding
+    const bool has_bias = bias_add || (n.in.size() > 2 && !n.in[2].empty());
+    if (bias_add) bias = *bias_add;
+    else if (has_bias) bias = lookup(g, n.in[2]);
     if (w.dtype != x.dtype) fail(LONNX_E_BADARG, "The weights tensor must be the same type as the input tensor.");
     if (x.shape.size() != 4) fail(LONNX_E_SHAPE, "The input tensor " + n.in[0] + " for parameter X has shape " + shape_str(x.shape) + " but is required to have rank 4.");
     if (w.shape.size() != 4) fail(LONNX_E_SHAPE, "The input tensor " + n.in[1] + " for parameter W has shape " + shape_str(w.shape) + " but is required to have rank 4.");
@@ -1193,6 +1196,8 @@ bool match_conv(Matcher &m, int i, Step &st) {
     return true;
 }
 
+bool channel_bias_shape(const Value &v, int64_t M);
+
 // Fused Conv step; false (nothing run) when the residual's shape differs
 // from the Conv output, so the nodes run one by one instead.
 bool exec_conv_step(lonnx_graph *g, const Step &s) {
@@ -1202,6 +1207,13 @@ bool exec_conv_step(lonnx_graph *g, const Step &s) {
         res = lookup(g, s.b);
         if (res.dtype != DT_FLOAT) return false;
         Value x = lookup(g, c.in.at(0)), w = lookup(g, c.in.at(1));
+        const bool conv_bias = c.in.size() > 2 && !c.in[2].empty();
+        if (!conv_bias && w.shape.size() == 4 && x.shape.size() == 4 && channel_bias_shape(res, w.shape[0])) {
+            ensure_dev(g, res);
+            const float *whi = s.wt ? (const float *)s.wt->p : nullptr;
+            const float *wlo = s.wlo ? (const float *)s.wlo->p : nullptr;
+            return exec_conv(g, c, s.epi, &s.y, nullptr, whi, wlo, s.w_tapmajor, &res);
+        }
         if (res.shape.size() != 4 || x.shape.size() != 4 || w.shape.size() != 4 || res.shape[0] != x.shape[0] ||
             res.shape[1] != w.shape[0])
             return false;  // exec_conv checks the full shape once it knows Ho, Wo
@@ -1209,6 +1221,16 @@ bool exec_conv_step(lonnx_graph *g, const Step &s) {
     }
     const float *whi = s.wt ? (const float *)s.wt->p : nullptr, *wlo = s.wlo ? (const float *)s.wlo->p : nullptr;
     return exec_conv(g, c, s.epi, &s.y, s.b.empty() ? nullptr : &res, whi, wlo, s.w_tapmajor);
+}
+
+// Conv -> Add(per-channel [.., M, 1, 1] operand) [-> Relu] with no conv bias:
+// the Add operand becomes the conv's bias.
+bool channel_bias_shape(const Value &v, int64_t M) {
+    const size_t r = v.shape.size();
+    if (r < 3 || v.shape[r - 1] != 1 || v.shape[r - 2] != 1 || v.shape[r - 3] != M) return false;
+    for (size_t d = 0; d + 3 < r; ++d)
+        if (v.shape[d] != 1) return false;
+    return true;
 }
 
 void build_steps(lonnx_graph *g, bool fuse) {
