@@ -228,3 +228,24 @@ def test_div_sqrt2_correctly_rounded(tmp_path):
     assert lib.mismatches(0x0D800000, 1, 1 << 23) == 0  # 2^-100 .. 2^-99
     assert lib.mismatches(0x80000000, 1, 1 << 23) == 0  # negative subnormals and tiny
     assert lib.mismatches(7, 997, (1 << 32) // 997) == 0
+
+
+def test_bench_reference_arm_contract():
+    """`bench.py --impl reference` (the reference's CPU algorithm through the
+    oracle restatement, no GPU) prints one JSON line with the bench contract:
+    the same metric and unit as the GPU arm, a cpu_baseline description and
+    an e2e block with zero host-device bytes."""
+    import json
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(root, "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "1"], capture_output=True, text=True, timeout=600, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
+    assert line["impl"] == "reference"
+    assert line["unit"] == "seq/s" and line["higher_is_better"] is True and line["value"] > 0
+    assert line["metric"].startswith("e5-small encoder throughput")
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == line["value"] and cb["sample"]
+    assert line["e2e"] == {"value": line["value"], "unit": "seq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
