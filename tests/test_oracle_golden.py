@@ -108,3 +108,44 @@ def test_mnist8_fixture_topology():
     assert g["opset"] == 8
     assert [n["op"] for n in g["nodes"]] == ["Reshape", "Conv", "Add", "Relu", "MaxPool", "Conv", "Add", "Relu",
                                              "MaxPool", "Reshape", "MatMul", "Add"]
+
+
+def test_broadcast_shape_reference_known_answers():
+    """tests/Lokad.Onnx.Tensors.Tests/ShapeTests.cs:24-45 (Tensor<int>.BroadcastShape),
+    through the oracle and through the library's host-side lonnx_broadcast_shape."""
+    import ctypes
+    cases = [((1, 1), (2,), (1, 2)), ((4, 1, 1), (2,), (4, 1, 2)), ((1, 2), (2,), (1, 2)),
+             ((1, 3), (2,), None), ((4, 3, 3), (2,), None), ((2, 1), (2,), (2, 2)), ((2, 1), (2, 3), (2, 3))]
+    try:
+        from onnx_b200 import _native as N
+    except ImportError:
+        N = None
+    for a, b, exp in cases:
+        assert O.broadcast_shape(a, b) == exp
+        if N is None:
+            continue
+        out = (ctypes.c_int64 * 8)()
+        r = ctypes.c_int()
+        rc = N.lib.lonnx_broadcast_shape(N.shape_arr(a), len(a), N.shape_arr(b), len(b), out, ctypes.byref(r))
+        if exp is None:
+            assert rc == -2
+        else:
+            assert rc == 0 and tuple(out[:r.value]) == exp
+
+
+def test_reshape_reference_known_answers():
+    """tests/Lokad.Onnx.Tensors.Tests/ShapeTests.cs:80-106 (Tensor<int>.Reshape):
+    explicit shapes, -1 inferred, 0 copies the input dimension."""
+    X = np.ones((2, 3, 4), np.int32)
+    for s, exp in [([4, 2, 3], (4, 2, 3)), ([2, 4, 3], (2, 4, 3)), ([2, 12], (2, 12)), ([2, -1, 2], (2, 6, 2)),
+                   ([-1, 2, 3, 4], (1, 2, 3, 4)), ([2, 0, 1, -1], (2, 3, 1, 4))]:
+        assert O.reshape(X, np.array(s, np.int64)).shape == exp
+
+
+def test_transpose_reference_known_answers():
+    """tests/Lokad.Onnx.Tensors.Tests/ShapeTests.cs:109-120: default reverses
+    the axes; an explicit permutation moves them."""
+    X = np.ones((2, 3, 4), np.int32)
+    assert O.transpose(X).shape[2] == 2
+    t = O.transpose(X, [2, 0, 1])
+    assert t.shape[0] == 4 and t.shape[2] == 3
