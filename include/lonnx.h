@@ -87,6 +87,15 @@ LONNX_API int lonnx_binary_f32(lonnx_ctx *ctx, int op, const float *a, const int
  * Tensor<float>.Relu/Sqrt/Erf (TensorOps.cs:1252,315,1353; MathOps.cs:989-1010). */
 LONNX_API int lonnx_unary_f32(lonnx_ctx *ctx, int op, const float *x, float *y, int64_t n);
 
+/* Inference BatchNormalization over axis 1 of an [outer, channels, inner]
+ * tensor: y = (x - mean[c]) / sqrt(var[c] + eps) * scale[c] + bias[c], each
+ * step rounded once in that order (ONNX BatchNormalization, opset 15).  The
+ * reference names the op (src/Lokad.Onnx.Base/OpType.cs:17) but has no
+ * implementation (CPUExecutionProvider.cs:24-50). */
+LONNX_API int lonnx_batchnorm_f32(lonnx_ctx *ctx, const float *x, const float *scale, const float *bias,
+                                  const float *mean, const float *var, float eps, float *y, int64_t outer,
+                                  int64_t channels, int64_t inner);
+
 /* ---- contractions ----------------------------------------------------------
  * C[b] = alpha * A[b] . op(B[b]) + beta * bias, then the epilogue.
  * A[b]: M x K row-major at A + b*strideA; B[b]: K x N (transB = 0) or N x K
@@ -104,15 +113,25 @@ LONNX_API int lonnx_gemm_f32(lonnx_ctx *ctx, const float *A, const float *B, con
  * allocate device memory (a host callback or a plugin inside a runtime that
  * owns the whole device pool, or code with no lonnx_ctx).  No counterpart in
  * the reference.  Work goes on `stream` (a cudaStream_t) of the current
- * device.  The tensor-core weight split uses a fixed 32 MiB file-scope device
- * array, so N * K must be <= 4194304 (else LONNX_E_BADARG).  All calls on a
- * device share that array: calls that overlap on the GPU race.  The first
- * call on a device resolves the array's address; make it before any stream
- * capture.  Expired device-side waits are not reported by this entry point. */
+ * device and is routed exactly as lonnx_gemm_f32 routes it.  Only the
+ * tensor-core path needs scratch: there the weight split uses a fixed 32 MiB
+ * file-scope device array, so N * K must be <= 4194304 (else
+ * LONNX_E_BADARG); the FFMA path (small, unaligned or LONNX_DISABLE_TC) has
+ * no limit.  All calls on a device share that array: calls that overlap on
+ * the GPU race.  The first call on a device clears the array's flag word
+ * synchronously; make it before any stream capture.  Expired device-side
+ * waits are recorded in sticky flags: read them with
+ * lonnx_gemm_f32_noalloc_status. */
 LONNX_API int lonnx_gemm_f32_noalloc(void *stream, const float *A, const float *B, const float *bias,
                                      float *C, int batch, int M, int N, int K, int64_t strideA,
                                      int64_t strideB, int64_t strideC, int transB, float alpha,
                                      float beta, int epilogue);
+/* Status of the lonnx_gemm_f32_noalloc calls on the current device since the
+ * last query: synchronises `stream`, reads and clears the shared flag word,
+ * and returns LONNX_E_TIMEOUT if any call's device-side pipeline wait
+ * expired (its C is then incomplete), else LONNX_OK.  Allocates nothing.  No
+ * counterpart in the reference. */
+LONNX_API int lonnx_gemm_f32_noalloc_status(void *stream);
 /* ONNX MatMul with numpy batch broadcasting on the leading dimensions
  * (Tensor<float>.MatMul, TensorOps.cs:600-704).  y has shape
  * broadcast(a[:-2], b[:-2]) + [a[-2], b[-1]]. */
@@ -191,6 +210,11 @@ LONNX_API int lonnx_graph_attr_int(lonnx_graph *g, const char *name, int64_t v);
 LONNX_API int lonnx_graph_attr_ints(lonnx_graph *g, const char *name, const int64_t *v, int n);
 LONNX_API int lonnx_graph_attr_float(lonnx_graph *g, const char *name, float v);
 LONNX_API int lonnx_graph_attr_string(lonnx_graph *g, const char *name, const char *v);
+LONNX_API int lonnx_graph_attr_floats(lonnx_graph *g, const char *name, const float *v, int n);
+/* A tensor-valued attribute (ONNX AttributeProto TENSOR, e.g. Constant's
+ * `value`); the data is copied. */
+LONNX_API int lonnx_graph_attr_tensor(lonnx_graph *g, const char *name, int dtype, const int64_t *shape,
+                                      int rank, const void *data);
 LONNX_API int lonnx_graph_add_output(lonnx_graph *g, const char *name);
 /* Opset of the model (selects attribute vs input forms, Node.cs:164-174). */
 LONNX_API int lonnx_graph_set_opset(lonnx_graph *g, int opset);
@@ -209,6 +233,8 @@ LONNX_API int lonnx_graph_execute(lonnx_graph *g);
 /* Shape of an output after execute: rank and dims (up to 8). */
 LONNX_API int lonnx_graph_output_shape(lonnx_graph *g, const char *name, int64_t *shape,
                                        int *rank);
+/* Element type (ONNX TensorProto code) of an output after execute. */
+LONNX_API int lonnx_graph_output_dtype(lonnx_graph *g, const char *name, int *dtype);
 LONNX_API int lonnx_graph_output_device(lonnx_graph *g, const char *name, const void **dev);
 /* Copy an output to host memory (bytes must equal the output's size). */
 LONNX_API int lonnx_graph_get_output(lonnx_graph *g, const char *name, void *host, size_t bytes);

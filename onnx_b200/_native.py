@@ -43,6 +43,7 @@ _SIGS = {
                                c_i64, c_int, c_f32, c_f32, c_int]),
     "lonnx_gemm_f32_noalloc": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_i64, c_i64,
                                        c_i64, c_int, c_f32, c_f32, c_int]),
+    "lonnx_gemm_f32_noalloc_status": (c_int, [c_vp]),
     "lonnx_matmul_f32": (c_int, [c_vp, c_vp, i64p, c_int, c_vp, i64p, c_int, c_vp]),
     "lonnx_conv2d_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp] + [c_int] * 17),
     "lonnx_softmax_f32": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64]),
@@ -52,6 +53,7 @@ _SIGS = {
     "lonnx_gather": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "lonnx_transpose": (c_int, [c_vp, c_vp, c_int, i64p, c_int, i64p, c_vp]),
     "lonnx_cast_i64_f32": (c_int, [c_vp, c_vp, c_vp, c_i64]),
+    "lonnx_batchnorm_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_f32, c_vp, c_i64, c_i64, c_i64]),
     "lonnx_attention_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_int, c_int, c_int,
                                     c_int, c_f32]),
     "lonnx_graph_create": (c_int, [c_vp, ctypes.POINTER(c_vp)]),
@@ -63,6 +65,8 @@ _SIGS = {
     "lonnx_graph_attr_ints": (c_int, [c_vp, c_char_p, i64p, c_int]),
     "lonnx_graph_attr_float": (c_int, [c_vp, c_char_p, c_f32]),
     "lonnx_graph_attr_string": (c_int, [c_vp, c_char_p, c_char_p]),
+    "lonnx_graph_attr_floats": (c_int, [c_vp, c_char_p, ctypes.POINTER(c_f32), c_int]),
+    "lonnx_graph_attr_tensor": (c_int, [c_vp, c_char_p, c_int, i64p, c_int, c_vp]),
     "lonnx_graph_add_output": (c_int, [c_vp, c_char_p]),
     "lonnx_graph_set_opset": (c_int, [c_vp, c_int]),
     "lonnx_graph_prepare": (c_int, [c_vp, c_int]),
@@ -70,6 +74,7 @@ _SIGS = {
     "lonnx_graph_set_input_device": (c_int, [c_vp, c_char_p, c_int, i64p, c_int, c_vp]),
     "lonnx_graph_execute": (c_int, [c_vp]),
     "lonnx_graph_output_shape": (c_int, [c_vp, c_char_p, i64p, ctypes.POINTER(c_int)]),
+    "lonnx_graph_output_dtype": (c_int, [c_vp, c_char_p, ctypes.POINTER(c_int)]),
     "lonnx_graph_output_device": (c_int, [c_vp, c_char_p, ctypes.POINTER(c_vp)]),
     "lonnx_graph_get_output": (c_int, [c_vp, c_char_p, c_vp, c_size]),
     "lonnx_graph_reset": (c_int, [c_vp]),

@@ -165,6 +165,34 @@ __global__ void k_cast_i64_f32(const int64_t *__restrict__ x, float *__restrict_
         y[i] = (float)x[i];
 }
 
+// Inference BatchNormalization over axis 1 of an [outer, C, inner] view, in
+// the ONNX formula's operation order with every step rounded once:
+// y = (x - mean) / sqrt(var + eps) * scale + B.  One CTA per (outer, c)
+// plane (grid-stride), threads across the plane, float4 when it is aligned.
+__global__ void k_batchnorm(const float *__restrict__ x, const float *__restrict__ scale,
+                            const float *__restrict__ bias, const float *__restrict__ mean,
+                            const float *__restrict__ var, float eps, float *__restrict__ y, int64_t planes,
+                            int64_t C, int64_t inner, bool vec4) {
+    for (int64_t p = blockIdx.x; p < planes; p += gridDim.x) {
+        const int64_t c = p % C;
+        const float m = mean[c], sc = scale[c], b = bias[c];
+        const float den = __fsqrt_rn(__fadd_rn(var[c], eps));
+        const float *xp = x + p * inner;
+        float *yp = y + p * inner;
+        auto f = [&](float v) { return __fadd_rn(__fmul_rn(__fdiv_rn(__fsub_rn(v, m), den), sc), b); };
+        if (vec4) {
+            const float4 *x4 = reinterpret_cast<const float4 *>(xp);
+            float4 *y4 = reinterpret_cast<float4 *>(yp);
+            for (int64_t i = threadIdx.x; i < inner / 4; i += blockDim.x) {
+                float4 u = __ldg(x4 + i);
+                y4[i] = make_float4(f(u.x), f(u.y), f(u.z), f(u.w));
+            }
+        } else {
+            for (int64_t i = threadIdx.x; i < inner; i += blockDim.x) yp[i] = f(xp[i]);
+        }
+    }
+}
+
 inline int grid_for(lonnx_ctx *ctx, int64_t work, int threads = 256) {
     int64_t blocks = (work + threads - 1) / threads;
     const int64_t cap = (int64_t)ctx->num_sms * 8;
@@ -346,6 +374,24 @@ LONNX_API int lonnx_unary_f32(lonnx_ctx *ctx, int op, const float *x, float *y, 
     case LONNX_GELU_ERF: k_unary<LONNX_GELU_ERF><<<g, T, 0, st>>>(x, y, n); break;
     default: return set_error(LONNX_E_BADARG, "unary: unknown op %d", op);
     }
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+LONNX_API int lonnx_batchnorm_f32(lonnx_ctx *ctx, const float *x, const float *scale, const float *bias,
+                                  const float *mean, const float *var, float eps, float *y, int64_t outer,
+                                  int64_t channels, int64_t inner) {
+    int rc = device_guard(ctx);
+    if (rc) return rc;
+    if (outer < 0 || channels < 0 || inner < 0) return set_error(LONNX_E_BADARG, "batchnorm: negative size");
+    const int64_t planes = outer * channels;
+    if (planes == 0 || inner == 0) return LONNX_OK;
+    if (!x || !scale || !bias || !mean || !var || !y) return set_error(LONNX_E_BADARG, "batchnorm: null tensor");
+    const bool vec4 = inner % 4 == 0 && aligned16(x) && aligned16(y);
+    const int threads = inner >= 1024 ? 256 : 128;
+    const int64_t cap = (int64_t)ctx->num_sms * 16;
+    k_batchnorm<<<(int)(planes < cap ? planes : cap), threads, 0, ctx->stream>>>(x, scale, bias, mean, var, eps, y,
+                                                                                 planes, channels, inner, vec4);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
 }

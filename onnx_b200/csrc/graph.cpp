@@ -99,11 +99,16 @@ struct Value {
 };
 
 struct Attr {
-    int kind = 0;  // 1 int, 2 ints, 3 float, 4 string
+    int kind = 0;  // 1 int, 2 ints, 3 float, 4 string, 5 floats, 6 tensor
     int64_t i = 0;
     std::vector<int64_t> ints;
     float f = 0;
+    std::vector<float> floats;
     std::string s;
+    // kind 6: a TensorProto-valued attribute (Constant's `value`)
+    int tdtype = 0;
+    std::vector<int64_t> tshape;
+    std::vector<uint8_t> tdata;
 };
 
 struct NodeDef {
@@ -132,6 +137,8 @@ struct Step {
     std::shared_ptr<DevBuf> bias;
     int N = 0, K = 0, epi = 0;
     int w_tapmajor = 0;  // conv: wt / wlo columns in (ky, kx, c) order (NHWC gather)
+    int wtrans = 0;          // GEMM from an ONNX Gemm: weight stored [N, K] (transB = 1)
+    float bias_beta = 1.0f;  // GEMM from an ONNX Gemm: the bias is beta * C
     std::vector<std::string> split_outputs;  // QKV: outputs per part (views), part width N/parts
     // LN
     std::string a, b;  // x (and residual) inputs
@@ -688,7 +695,19 @@ void exec_shape(lonnx_graph *g, const NodeDef &n) {
 
 void exec_constant(lonnx_graph *g, const NodeDef &n) {
     Value y;
-    if (const Attr *a = n.get("value_float")) {
+    if (const Attr *a = n.get("value"); a && a->kind == 6) {
+        y.dtype = a->tdtype;
+        y.shape = a->tshape;
+        y.host = std::make_shared<std::vector<uint8_t>>(a->tdata);
+        if (y.host->size() != y.bytes()) fail(LONNX_E_BADARG, "Constant: value tensor size mismatch");
+        if (y.dtype == DT_FLOAT) ensure_dev(g, y);
+    } else if (const Attr *a = n.get("value_floats")) {
+        y.dtype = DT_FLOAT;
+        y.shape = {(int64_t)a->floats.size()};
+        y.host = std::make_shared<std::vector<uint8_t>>(a->floats.size() * 4);
+        if (!a->floats.empty()) memcpy(y.host->data(), a->floats.data(), a->floats.size() * 4);
+        ensure_dev(g, y);
+    } else if (const Attr *a = n.get("value_float")) {
         y.dtype = DT_FLOAT;
         y.host = std::make_shared<std::vector<uint8_t>>(4);
         memcpy(y.host->data(), &a->f, 4);
@@ -802,6 +821,151 @@ void exec_slice(lonnx_graph *g, const NodeDef &n) {
     g->env[n.out.at(0)] = y;
 }
 
+// ---------------------------------------------------------------------------
+// ONNX ops the reference names (OpType.cs) but does not dispatch
+// (CPUExecutionProvider.cs:24-50): Gemm, BatchNormalization,
+// GlobalAveragePool, Flatten, plus the inference no-ops Identity and
+// Dropout.  Semantics follow the ONNX operator specification.
+
+float attr_float(const NodeDef &n, const char *name, float d) {
+    const Attr *a = n.get(name);
+    if (!a) return d;
+    return a->kind == 3 ? a->f : (float)a->i;
+}
+
+int64_t attr_int(const NodeDef &n, const char *name, int64_t d) {
+    const Attr *a = n.get(name);
+    return a && a->kind == 1 ? a->i : d;
+}
+
+Value device_scalar(lonnx_graph *g, float v) {
+    Value s;
+    s.dtype = DT_FLOAT;
+    s.host = std::make_shared<std::vector<uint8_t>>(4);
+    memcpy(s.host->data(), &v, 4);
+    ensure_dev(g, s);
+    return s;
+}
+
+// Y = alpha * op(A) . op(B) + beta * C, C unidirectionally broadcast to [M, N]
+void exec_gemm(lonnx_graph *g, const NodeDef &n) {
+    Value a = lookup(g, n.in.at(0)), b = lookup(g, n.in.at(1));
+    if (a.dtype != DT_FLOAT || b.dtype != DT_FLOAT) fail(LONNX_E_UNSUPPORTED, "Gemm: only float tensors are supported on the device");
+    if (a.shape.size() != 2) fail(LONNX_E_SHAPE, "The input tensor " + n.in[0] + " for parameter A has shape " + shape_str(a.shape) + " but is required to have rank 2.");
+    if (b.shape.size() != 2) fail(LONNX_E_SHAPE, "The input tensor " + n.in[1] + " for parameter B has shape " + shape_str(b.shape) + " but is required to have rank 2.");
+    const float alpha = attr_float(n, "alpha", 1.0f), beta = attr_float(n, "beta", 1.0f);
+    const bool ta = attr_int(n, "transA", 0) != 0, tb = attr_int(n, "transB", 0) != 0;
+    const int64_t M = ta ? a.shape[1] : a.shape[0], K = ta ? a.shape[0] : a.shape[1];
+    const int64_t Kb = tb ? b.shape[1] : b.shape[0], N = tb ? b.shape[0] : b.shape[1];
+    if (K != Kb) fail(LONNX_E_SHAPE, "Gemm: inner dimensions " + shape_str(a.shape) + " and " + shape_str(b.shape) + " do not match.");
+    if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) fail(LONNX_E_UNSUPPORTED, "Gemm: dimension too large");
+    ensure_dev(g, a);
+    ensure_dev(g, b);
+    const float *A = (const float *)a.dptr();
+    Value at;
+    if (ta) {
+        at = new_dev(g, DT_FLOAT, {M, K});
+        const int64_t perm[2] = {1, 0};
+        ck(lonnx_transpose(g->ctx, a.dptr(), 4, a.shape.data(), 2, perm, at.dptr_mut()));
+        A = (const float *)at.dptr();
+    }
+    const bool has_c = n.in.size() > 2 && !n.in[2].empty();
+    Value c;
+    bool row_bias = false;
+    if (has_c) {
+        c = lookup(g, n.in[2]);
+        if (c.dtype != DT_FLOAT) fail(LONNX_E_BADARG, "Gemm: C must be a float tensor");
+        ensure_dev(g, c);
+        row_bias = c.numel() == N && (c.shape.size() == 1 || (c.shape.size() == 2 && c.shape[0] == 1));
+        int64_t os[8];
+        int orank = 0;
+        const int64_t mn[2] = {M, N};
+        if (c.shape.size() > 2 || lonnx_broadcast_shape(c.shape.data(), (int)c.shape.size(), mn, 2, os, &orank) ||
+            orank != 2 || os[0] != M || os[1] != N)
+            fail(LONNX_E_SHAPE, "Gemm: C of shape " + shape_str(c.shape) + " does not broadcast to " + shape_str({M, N}));
+    }
+    Value y = new_dev(g, DT_FLOAT, {M, N});
+    ck(lonnx_gemm_f32(g->ctx, A, (const float *)b.dptr(), row_bias ? (const float *)c.dptr() : nullptr,
+                      (float *)y.dptr_mut(), 1, (int)M, (int)N, (int)K, 0, 0, 0, tb ? 1 : 0, alpha,
+                      row_bias ? beta : 0.0f, LONNX_EPI_NONE));
+    if (has_c && !row_bias && beta != 0.0f) {
+        Value cb = c;
+        if (beta != 1.0f) {
+            Value bs = device_scalar(g, beta);
+            cb = new_dev(g, DT_FLOAT, c.shape);
+            ck(lonnx_binary_f32(g->ctx, LONNX_MUL, (const float *)c.dptr(), c.shape.data(), (int)c.shape.size(),
+                                (const float *)bs.dptr(), nullptr, 0, (float *)cb.dptr_mut()));
+        }
+        Value y2 = new_dev(g, DT_FLOAT, {M, N});
+        ck(lonnx_binary_f32(g->ctx, LONNX_ADD, (const float *)y.dptr(), y.shape.data(), 2, (const float *)cb.dptr(),
+                            cb.shape.data(), (int)cb.shape.size(), (float *)y2.dptr_mut()));
+        y = y2;
+    }
+    g->env[n.out.at(0)] = y;
+}
+
+// mean over every spatial axis (2 .. rank-1), keeping them as 1s
+void exec_global_avg_pool(lonnx_graph *g, const NodeDef &n) {
+    Value x = lookup(g, n.in.at(0));
+    if (x.dtype != DT_FLOAT) fail(LONNX_E_UNSUPPORTED, "GlobalAveragePool: only float tensors are supported");
+    const int rank = (int)x.shape.size();
+    if (rank < 3) fail(LONNX_E_SHAPE, "The input tensor " + n.in[0] + " for parameter X has shape " + shape_str(x.shape) + " but is required to have rank >= 3.");
+    std::vector<int64_t> axes, oshape(x.shape.begin(), x.shape.begin() + 2);
+    for (int d = 2; d < rank; ++d) { axes.push_back(d); oshape.push_back(1); }
+    ensure_dev(g, x);
+    Value y = new_dev(g, DT_FLOAT, oshape);
+    ck(lonnx_reduce_f32(g->ctx, LONNX_REDUCE_MEAN, (const float *)x.dptr(), x.shape.data(), rank, axes.data(),
+                        (int)axes.size(), (float *)y.dptr_mut()));
+    g->env[n.out.at(0)] = y;
+}
+
+void exec_flatten(lonnx_graph *g, const NodeDef &n) {
+    Value x = lookup(g, n.in.at(0));
+    const int64_t rank = (int64_t)x.shape.size();
+    int64_t axis = norm_axis(attr_int(n, "axis", 1), rank);
+    if (axis < 0 || axis > rank) fail(LONNX_E_BADARG, "Flatten: axis out of range");
+    int64_t outer = 1;
+    for (int64_t d = 0; d < axis; ++d) outer *= x.shape[d];
+    Value y = x;  // zero-copy view
+    y.shape = {outer, outer ? x.numel() / outer : 0};
+    g->env[n.out.at(0)] = y;
+}
+
+// inference-mode BatchNormalization over axis 1
+void exec_batchnorm(lonnx_graph *g, const NodeDef &n) {
+    if (n.in.size() < 5) fail(LONNX_E_BADARG, "BatchNormalization needs X, scale, B, input_mean and input_var");
+    if (attr_int(n, "training_mode", 0)) fail(LONNX_E_UNSUPPORTED, "BatchNormalization: training_mode is not supported");
+    Value x = lookup(g, n.in[0]);
+    Value p[4] = {lookup(g, n.in[1]), lookup(g, n.in[2]), lookup(g, n.in[3]), lookup(g, n.in[4])};
+    if (x.dtype != DT_FLOAT || x.shape.size() < 2) fail(LONNX_E_SHAPE, "BatchNormalization: X must be a float tensor of rank >= 2");
+    const int64_t C = x.shape[1];
+    for (auto &v : p) {
+        if (v.dtype != DT_FLOAT || v.numel() != C) fail(LONNX_E_SHAPE, "BatchNormalization: parameters must hold one float per channel");
+        ensure_dev(g, v);
+    }
+    int64_t inner = 1;
+    for (size_t d = 2; d < x.shape.size(); ++d) inner *= x.shape[d];
+    ensure_dev(g, x);
+    Value y = new_dev(g, DT_FLOAT, x.shape);
+    ck(lonnx_batchnorm_f32(g->ctx, (const float *)x.dptr(), (const float *)p[0].dptr(), (const float *)p[1].dptr(),
+                           (const float *)p[2].dptr(), (const float *)p[3].dptr(), attr_float(n, "epsilon", 1e-5f),
+                           (float *)y.dptr_mut(), x.shape[0], C, inner));
+    g->env[n.out.at(0)] = y;
+}
+
+// Identity, and Dropout at inference (output = input, mask = all true)
+void exec_identity(lonnx_graph *g, const NodeDef &n) {
+    Value x = lookup(g, n.in.at(0));
+    g->env[n.out.at(0)] = x;
+    if (n.out.size() > 1 && !n.out[1].empty()) {
+        Value m;
+        m.dtype = DT_BOOL;
+        m.shape = x.shape;
+        m.host = std::make_shared<std::vector<uint8_t>>(m.bytes(), 1);
+        g->env[n.out[1]] = m;
+    }
+}
+
 void exec_node(lonnx_graph *g, const NodeDef &n) {
     const std::string &op = n.op;
     if (op == "Add" || op == "Sub" || op == "Mul" || op == "Div" || op == "Pow") return exec_binary(g, n);
@@ -822,6 +986,11 @@ void exec_node(lonnx_graph *g, const NodeDef &n) {
     if (op == "Constant") return exec_constant(g, n);
     if (op == "Concat") return exec_concat(g, n);
     if (op == "Slice") return exec_slice(g, n);
+    if (op == "Gemm") return exec_gemm(g, n);
+    if (op == "GlobalAveragePool") return exec_global_avg_pool(g, n);
+    if (op == "Flatten") return exec_flatten(g, n);
+    if (op == "BatchNormalization") return exec_batchnorm(g, n);
+    if (op == "Identity" || op == "Dropout") return exec_identity(g, n);
     fail(LONNX_E_UNSUPPORTED, "The operation " + op + " is not supported by the backend.");
 }
 
@@ -1171,6 +1340,41 @@ bool match_attn(Matcher &m, int i, Step &st, std::vector<int> &heads_nodes) {
     return true;
 }
 
+// ONNX Gemm(A, W, C) with W an initializer, transA = 0, alpha = 1 and C
+// absent or a row bias [N] / [1, N] initializer: one GEMM step (beta folded
+// into the bias, transB into the weight split)
+bool match_gemm_onnx(Matcher &m, int i, Step &st) {
+    const NodeDef &gm = m.N(i);
+    if (gm.op != "Gemm" || gm.in.size() < 2 || !m.is_init(gm.in[1])) return false;
+    if (attr_int(gm, "transA", 0) != 0 || attr_float(gm, "alpha", 1.0f) != 1.0f) return false;
+    const Value &W = m.g->inits.at(gm.in[1]);
+    if (W.dtype != DT_FLOAT || W.shape.size() != 2) return false;
+    const int tb = attr_int(gm, "transB", 0) ? 1 : 0;
+    const int64_t K = tb ? W.shape[1] : W.shape[0], N = tb ? W.shape[0] : W.shape[1];
+    if (K > INT32_MAX || N > INT32_MAX) return false;
+    std::string bname;
+    if (gm.in.size() > 2 && !gm.in[2].empty()) {
+        bname = gm.in[2];
+        if (!m.is_init(bname)) return false;
+        const Value &b = m.g->inits.at(bname);
+        if (b.dtype != DT_FLOAT || b.numel() != N || !(b.shape.size() == 1 || (b.shape.size() == 2 && b.shape[0] == 1)))
+            return false;
+    }
+    st = Step();
+    st.kind = S_GEMM;
+    st.nodes = {i};
+    st.x = gm.in[0];
+    st.y = gm.out[0];
+    st.K = (int)K;
+    st.N = (int)N;
+    st.epi = LONNX_EPI_NONE;
+    st.a = gm.in[1];
+    st.b = bname;
+    st.wtrans = tb;
+    st.bias_beta = attr_float(gm, "beta", 1.0f);
+    return true;
+}
+
 // Conv [-> Add(residual)] [-> Relu]: each intermediate used only by the next node
 bool match_conv(Matcher &m, int i, Step &st) {
     const NodeDef &c = m.N(i);
@@ -1233,8 +1437,74 @@ bool channel_bias_shape(const Value &v, int64_t M) {
     return true;
 }
 
+Value make_value(lonnx_graph *g, int dtype, const int64_t *shape, int rank, const void *host, bool upload);
+
+// Conv (initializer weight, optional initializer bias) -> BatchNormalization
+// (initializer parameters, the conv output used by nothing else): the BN is
+// folded into the conv once, W' = W * s and b' = (b - mean) * s + B with
+// s = scale / sqrt(var + eps) (computed in double, rounded once), and the BN
+// node is removed.  The conv then fuses with a following Add / Relu as usual.
+void fold_batchnorm(lonnx_graph *g) {
+    std::map<std::string, int> uses, producer;
+    for (size_t j = 0; j < g->nodes.size(); ++j) {
+        for (auto &in : g->nodes[j].in) uses[in]++;
+        for (auto &o : g->nodes[j].out) producer[o] = (int)j;
+    }
+    const std::set<std::string> outs(g->outputs.begin(), g->outputs.end());
+    std::vector<bool> drop(g->nodes.size(), false);
+    auto init_f32 = [&](const std::string &name, int64_t numel, std::vector<float> *out) {
+        auto it = g->inits.find(name);
+        if (it == g->inits.end() || it->second.dtype != DT_FLOAT || it->second.numel() != numel) return false;
+        Value v = it->second;
+        ensure_host(g, v);
+        out->assign(v.h<float>(), v.h<float>() + numel);
+        return true;
+    };
+    for (size_t j = 0; j < g->nodes.size(); ++j) {
+        const NodeDef &bn = g->nodes[j];
+        if (bn.op != "BatchNormalization" || bn.in.size() < 5 || attr_int(bn, "training_mode", 0)) continue;
+        bool extra_out = false;
+        for (size_t k = 1; k < bn.out.size(); ++k) extra_out |= !bn.out[k].empty();
+        if (extra_out) continue;
+        auto pi = producer.find(bn.in[0]);
+        if (pi == producer.end() || uses[bn.in[0]] != 1 || outs.count(bn.in[0])) continue;
+        NodeDef &cv = g->nodes[pi->second];
+        if (cv.op != "Conv" || cv.in.size() < 2 || !g->inits.count(cv.in[1])) continue;
+        const Value &W = g->inits.at(cv.in[1]);
+        if (W.dtype != DT_FLOAT || W.shape.size() != 4) continue;
+        const int64_t M = W.shape[0], per = W.numel() / std::max<int64_t>(M, 1);
+        std::vector<float> w, b(M, 0.0f), sc, bb, mean, var;
+        const bool has_b = cv.in.size() > 2 && !cv.in[2].empty();
+        if (has_b && !init_f32(cv.in[2], M, &b)) continue;
+        if (!init_f32(bn.in[1], M, &sc) || !init_f32(bn.in[2], M, &bb) || !init_f32(bn.in[3], M, &mean) ||
+            !init_f32(bn.in[4], M, &var) || !init_f32(cv.in[1], W.numel(), &w))
+            continue;
+        const double eps = attr_float(bn, "epsilon", 1e-5f);
+        std::vector<float> wf(w.size()), bf(M);
+        for (int64_t m = 0; m < M; ++m) {
+            const double s = (double)sc[m] / sqrt((double)var[m] + eps);
+            for (int64_t k = 0; k < per; ++k) wf[m * per + k] = (float)((double)w[m * per + k] * s);
+            bf[m] = (float)(((double)b[m] - (double)mean[m]) * s + (double)bb[m]);
+        }
+        const std::string wn = "__bnfold__/" + bn.out[0] + "/W", bname = "__bnfold__/" + bn.out[0] + "/B";
+        g->inits[wn] = make_value(g, DT_FLOAT, W.shape.data(), 4, wf.data(), true);
+        const int64_t bshape[1] = {M};
+        g->inits[bname] = make_value(g, DT_FLOAT, bshape, 1, bf.data(), true);
+        cv.in.resize(3);
+        cv.in[1] = wn;
+        cv.in[2] = bname;
+        cv.out[0] = bn.out[0];
+        drop[j] = true;
+    }
+    std::vector<NodeDef> kept;
+    for (size_t j = 0; j < g->nodes.size(); ++j)
+        if (!drop[j]) kept.push_back(std::move(g->nodes[j]));
+    g->nodes.swap(kept);
+}
+
 void build_steps(lonnx_graph *g, bool fuse) {
     g->steps.clear();
+    if (fuse) fold_batchnorm(g);
     const int n = (int)g->nodes.size();
     if (!fuse) {
         for (int i = 0; i < n; ++i) {
@@ -1264,7 +1534,7 @@ void build_steps(lonnx_graph *g, bool fuse) {
     for (int i = 0; i < n; ++i) {
         if (m.used[i]) continue;
         Step st;
-        if (match_gemm(m, i, st)) { claim(st); continue; }
+        if (match_gemm(m, i, st) || match_gemm_onnx(m, i, st)) { claim(st); continue; }
     }
     for (int i = 0; i < n; ++i) {
         if (m.used[i]) continue;
@@ -1282,9 +1552,20 @@ void build_steps(lonnx_graph *g, bool fuse) {
         const Value &W = g->inits.at(st.a);
         st.wt = std::make_shared<DevBuf>(g->ctx, (size_t)st.N * st.K * 4);
         st.wlo = std::make_shared<DevBuf>(g->ctx, (size_t)st.N * st.K * 4);
-        ck(split_tf32_nk(g->ctx, (const float *)W.dptr(), (float *)st.wt->p, (float *)st.wlo->p, st.K, st.N, 0));
-        const Value &B = g->inits.at(st.b);
-        st.bias = B.buf;
+        ck(split_tf32_nk(g->ctx, (const float *)W.dptr(), (float *)st.wt->p, (float *)st.wlo->p, st.K, st.N,
+                         st.wtrans));
+        if (st.b.empty()) {
+            st.bias = nullptr;
+        } else if (st.bias_beta == 1.0f) {
+            st.bias = g->inits.at(st.b).buf;
+        } else {
+            Value B = g->inits.at(st.b);
+            ensure_host(g, B);
+            std::vector<float> scaled(st.N);
+            for (int j = 0; j < st.N; ++j) scaled[j] = st.bias_beta * B.h<float>()[j];
+            st.bias = std::make_shared<DevBuf>(g->ctx, (size_t)st.N * 4);
+            ck(lonnx_memcpy_h2d(g->ctx, st.bias->p, scaled.data(), (size_t)st.N * 4));
+        }
     }
     // conv weights [M, C, kh, kw] = [M, K] -> tf32 hi / lo [M, ldk] once
     for (auto &st : groups) {
@@ -1581,6 +1862,37 @@ LONNX_API int lonnx_graph_attr_string(lonnx_graph *g, const char *name, const ch
     return LONNX_OK;
 }
 
+LONNX_API int lonnx_graph_attr_floats(lonnx_graph *g, const char *name, const float *v, int cnt) {
+    NodeDef *n = last_node(g);
+    if (!n || !name || cnt < 0 || (cnt && !v)) return set_error(LONNX_E_BADARG, "no node");
+    Attr a;
+    a.kind = 5;
+    a.floats.assign(v, v + cnt);
+    n->attrs[name] = a;
+    return LONNX_OK;
+}
+
+LONNX_API int lonnx_graph_attr_tensor(lonnx_graph *g, const char *name, int dtype, const int64_t *shape, int rank,
+                                      const void *data) {
+    NodeDef *n = last_node(g);
+    if (!n || !name || rank < 0 || rank > 8 || (rank && !shape)) return set_error(LONNX_E_BADARG, "no node");
+    if (!dtype_size(dtype)) return set_error(LONNX_E_UNSUPPORTED, "unsupported dtype %d", dtype);
+    Attr a;
+    a.kind = 6;
+    a.tdtype = dtype;
+    a.tshape.assign(shape, shape + rank);
+    int64_t cnt = 1;
+    for (auto d : a.tshape) {
+        if (d < 0) return set_error(LONNX_E_BADARG, "negative dimension");
+        cnt *= d;
+    }
+    const size_t bytes = (size_t)cnt * dtype_size(dtype);
+    if (bytes && !data) return set_error(LONNX_E_BADARG, "null tensor data");
+    a.tdata.assign((const uint8_t *)data, (const uint8_t *)data + bytes);
+    n->attrs[name] = a;
+    return LONNX_OK;
+}
+
 LONNX_API int lonnx_graph_add_output(lonnx_graph *g, const char *name) {
     if (!g || !name) return set_error(LONNX_E_BADARG, "null argument");
     g->outputs.push_back(name);
@@ -1648,6 +1960,14 @@ LONNX_API int lonnx_graph_output_shape(lonnx_graph *g, const char *name, int64_t
         const Value &v = lookup(g, name);
         *rank = (int)v.shape.size();
         for (size_t i = 0; i < v.shape.size(); ++i) shape[i] = v.shape[i];
+        return LONNX_OK;
+    });
+}
+
+LONNX_API int lonnx_graph_output_dtype(lonnx_graph *g, const char *name, int *dtype) {
+    if (!g || !name || !dtype) return set_error(LONNX_E_BADARG, "null argument");
+    return guarded([&] {
+        *dtype = lookup(g, name).dtype;
         return LONNX_OK;
     });
 }

@@ -24,6 +24,31 @@ def _cstrs(names):
     return arr
 
 
+def _set_attr(g, k, v):
+    """One attribute of the last added node, by Python type: str, float,
+    int, list of ints / floats, or a numpy array (a TENSOR attribute)."""
+    name = k.encode()
+    if isinstance(v, str):
+        N.check(N.lib.lonnx_graph_attr_string(g, name, v.encode()))
+    elif isinstance(v, np.ndarray):
+        a = np.ascontiguousarray(v)
+        if a.dtype == np.float64:
+            a = a.astype(np.float32)
+        N.check(N.lib.lonnx_graph_attr_tensor(g, name, ONNX_DTYPE[a.dtype], N.shape_arr(a.shape), a.ndim,
+                                              a.ctypes.data))
+    elif isinstance(v, (float, np.floating)):
+        N.check(N.lib.lonnx_graph_attr_float(g, name, float(v)))
+    elif isinstance(v, (list, tuple)):
+        if v and isinstance(v[0], (float, np.floating)):
+            arr = (ctypes.c_float * len(v))(*[float(x) for x in v])
+            N.check(N.lib.lonnx_graph_attr_floats(g, name, arr, len(v)))
+        else:
+            arr = (ctypes.c_int64 * max(len(v), 1))(*[int(x) for x in v])
+            N.check(N.lib.lonnx_graph_attr_ints(g, name, arr, len(v)))
+    else:
+        N.check(N.lib.lonnx_graph_attr_int(g, name, int(v)))
+
+
 class ComputationalGraph:
     """A GraphDef loaded onto one GPU."""
 
@@ -47,22 +72,19 @@ class ComputationalGraph:
             N.check(N.lib.lonnx_graph_add_node(g, node.op.encode(), _cstrs(node.inputs), len(node.inputs),
                                                _cstrs(node.outputs), len(node.outputs)))
             for k, v in node.attrs.items():
-                if isinstance(v, str):
-                    N.check(N.lib.lonnx_graph_attr_string(g, k.encode(), v.encode()))
-                elif isinstance(v, float):
-                    N.check(N.lib.lonnx_graph_attr_float(g, k.encode(), v))
-                elif isinstance(v, (list, tuple)):
-                    if v and isinstance(v[0], float):
-                        raise ValueError(f"float-list attribute {k} is not supported")
-                    arr = (ctypes.c_int64 * max(len(v), 1))(*[int(x) for x in v])
-                    N.check(N.lib.lonnx_graph_attr_ints(g, k.encode(), arr, len(v)))
-                else:
-                    N.check(N.lib.lonnx_graph_attr_int(g, k.encode(), int(v)))
+                _set_attr(g, k, v)
         for o in graph.outputs:
             N.check(N.lib.lonnx_graph_add_output(g, o.encode()))
         flags = (1 if fuse else 0) | (2 if honor_conv_attrs else 0)
         N.check(N.lib.lonnx_graph_prepare(g, flags))
         self._device_inputs = []
+
+    @classmethod
+    def load(cls, path: str, ctx: Context | None = None, **kw) -> "ComputationalGraph":
+        """Model.Load (src/Lokad.Onnx.Backend/Model.cs:30-63): read a .onnx
+        file and load its graph onto the GPU."""
+        from . import onnx_io
+        return cls(onnx_io.load(path), ctx, **kw)
 
     @property
     def num_steps(self) -> int:
@@ -100,8 +122,13 @@ class ComputationalGraph:
         N.check(N.lib.lonnx_graph_output_shape(self.handle, name.encode(), shp, ctypes.byref(r)))
         return tuple(shp[i] for i in range(r.value))
 
-    def output(self, name, dtype=np.float32) -> np.ndarray:
-        out = np.empty(self.output_shape(name), dtype)
+    def output_dtype(self, name) -> np.dtype:
+        d = ctypes.c_int()
+        N.check(N.lib.lonnx_graph_output_dtype(self.handle, name.encode(), ctypes.byref(d)))
+        return NP_DTYPE[d.value]
+
+    def output(self, name, dtype=None) -> np.ndarray:
+        out = np.empty(self.output_shape(name), dtype or self.output_dtype(name))
         N.check(N.lib.lonnx_graph_get_output(self.handle, name.encode(), out.ctypes.data, out.nbytes))
         return out
 
@@ -128,27 +155,14 @@ class ComputationalGraph:
 
 
 def run_node(node: Node, inputs: dict, ctx: Context | None = None, opset: int = 13,
-             initializers: dict | None = None) -> dict:
+             initializers: dict | None = None, honor_conv_attrs: bool = False) -> dict:
     """Execute one node on the GPU (the reference's backend.run_node form):
-    ``inputs`` maps the node's input names to host arrays; returns name -> array."""
+    ``inputs`` maps the node's input names to host arrays; returns name -> array
+    (each output in the element type the executor produced)."""
     inits = dict(initializers or {})
-    gd = GraphDef([node], inits, [n for n in node.inputs if n and n not in inits], list(node.outputs), opset)
-    g = ComputationalGraph(gd, ctx, fuse=False)
+    outs = [o for o in node.outputs if o]
+    gd = GraphDef([node], inits, [n for n in node.inputs if n and n not in inits], outs, opset)
+    g = ComputationalGraph(gd, ctx, fuse=False, honor_conv_attrs=honor_conv_attrs)
     g.set_inputs({k: v for k, v in inputs.items()})
     g.run()
-    res = {}
-    for o in node.outputs:
-        shp = g.output_shape(o)
-        dt = np.float32
-        # outputs keep the dtype of their producing op: integer for shape ops / int gathers
-        if node.op in ("Shape",):
-            dt = np.int64
-        elif node.op in ("Gather", "Reshape", "Unsqueeze", "Transpose", "Concat", "Slice") and inputs:
-            first = inputs.get(node.inputs[0], inits.get(node.inputs[0]))
-            dt = np.asarray(first).dtype
-        elif node.op == "Cast":
-            dt = NP_DTYPE[int(node.attrs["to"])]
-        out = np.empty(shp, dt)
-        N.check(N.lib.lonnx_graph_get_output(g.handle, o.encode(), out.ctypes.data, out.nbytes))
-        res[o] = out
-    return res
+    return {o: g.output(o) for o in outs}

@@ -222,14 +222,24 @@ def e5_flops_per_seq(layers=12, hidden=384, ffn=1536, seq=128):
                      + 2 * 2 * seq * seq * hidden)
 
 
-def resnet50(num_classes=1000, seed=0) -> GraphDef:
-    """ResNet-50 v1: stride on the first 1x1 of each
-    downsampling bottleneck, BatchNorm folded into each conv's weight scale and
-    bias (Kaiming-normal weights; the folded BN scale is 0.2 on the last conv
-    of each residual branch and 0.5 on projection shortcuts, which keeps
-    activations O(1) through the 16 residual sums as trained BNs do), global average pool as ReduceMean over H and W,
-    final 2048 x num_classes MatMul + bias.  Convs carry explicit
-    strides/pads; run them with the attributes applied
+def resnet50(num_classes=1000, seed=0, onnx_ops=False) -> GraphDef:
+    """ResNet-50 v1: stride on the first 1x1 of each downsampling bottleneck,
+    Kaiming-normal conv weights, global average pool, final 2048 x
+    num_classes classifier.
+
+    onnx_ops=False: BatchNorm folded into each conv's weight scale and bias
+    (the folded BN scale is 0.2 on the last conv of each residual branch and
+    0.5 on projection shortcuts, which keeps activations O(1) through the 16
+    residual sums as trained BNs do), global average pool as ReduceMean over
+    H and W, classifier as MatMul + bias Add -- only ops the reference
+    dispatches.
+
+    onnx_ops=True: the graph as an ONNX export of torchvision's ResNet-50
+    lays it out -- Conv without bias -> BatchNormalization (seeded
+    scale/B/mean/var, same per-branch damping) -> Relu, GlobalAveragePool,
+    Flatten, Gemm(transB=1) -- the ops the reference names but cannot run.
+
+    Convs carry explicit strides/pads; run them with the attributes applied
     (ComputationalGraph(..., honor_conv_attrs=True)), which the reference's
     Conv dispatch does not do (Node.cs:137-138)."""
     rng = np.random.default_rng(seed)
@@ -240,13 +250,27 @@ def resnet50(num_classes=1000, seed=0) -> GraphDef:
         i = cnt[0]
         cnt[0] += 1
         w, b = f"conv{i}.w", f"conv{i}.b"
-        std = gamma * np.sqrt(2.0 / (cin * k * k))
-        inits[w] = (rng.standard_normal((cout, cin, k, k), dtype=np.float32) * std).astype(np.float32)
-        inits[b] = (rng.standard_normal(cout, dtype=np.float32) * 0.01).astype(np.float32)
+        attrs = {"kernel_shape": [k, k], "strides": [s, s], "pads": [pad] * 4, "auto_pad": "NOTSET", "group": 1,
+                 "dilations": [1, 1]}
         y = f"conv{i}.y"
-        nodes.append(Node("Conv", [x, w, b], [y], {"kernel_shape": [k, k], "strides": [s, s],
-                                                    "pads": [pad] * 4, "auto_pad": "NOTSET", "group": 1,
-                                                    "dilations": [1, 1]}))
+        if not onnx_ops:
+            std = gamma * np.sqrt(2.0 / (cin * k * k))
+            inits[w] = (rng.standard_normal((cout, cin, k, k), dtype=np.float32) * std).astype(np.float32)
+            inits[b] = (rng.standard_normal(cout, dtype=np.float32) * 0.01).astype(np.float32)
+            nodes.append(Node("Conv", [x, w, b], [y], attrs))
+        else:
+            std = np.sqrt(2.0 / (cin * k * k))
+            inits[w] = (rng.standard_normal((cout, cin, k, k), dtype=np.float32) * std).astype(np.float32)
+            bn = f"bn{i}"
+            mean = (rng.standard_normal(cout, dtype=np.float32) * 0.1).astype(np.float32)
+            var = rng.uniform(0.5, 1.5, cout).astype(np.float32)
+            inits[bn + ".scale"] = (gamma * np.sqrt(var + 1e-5) * rng.uniform(0.9, 1.1, cout)).astype(np.float32)
+            inits[bn + ".B"] = (rng.standard_normal(cout, dtype=np.float32) * 0.01).astype(np.float32)
+            inits[bn + ".mean"] = mean
+            inits[bn + ".var"] = var
+            nodes.append(Node("Conv", [x, w], [y + ".pre"], attrs))
+            nodes.append(Node("BatchNormalization", [y + ".pre", bn + ".scale", bn + ".B", bn + ".mean", bn + ".var"],
+                              [y], {"epsilon": 1e-5}))
         if relu:
             nodes.append(Node("Relu", [y], [y + ".relu"]))
             return y + ".relu"
@@ -268,12 +292,21 @@ def resnet50(num_classes=1000, seed=0) -> GraphDef:
             nodes.append(Node("Add", [h, sc], [name + ".sum"]))
             nodes.append(Node("Relu", [name + ".sum"], [name]))
             x, cin = name, cout
-    inits["gap_axes"] = np.array([2, 3], np.int64)
-    nodes.append(Node("ReduceMean", [x, "gap_axes"], ["gap"], {"keepdims": 0}))
-    inits["fc.w"] = (rng.standard_normal((2048, num_classes), dtype=np.float32) * np.sqrt(1.0 / 2048)).astype(np.float32)
-    inits["fc.b"] = np.zeros(num_classes, np.float32)
-    nodes.append(Node("MatMul", ["gap", "fc.w"], ["fc.mm"]))
-    nodes.append(Node("Add", ["fc.mm", "fc.b"], ["logits"]))
+    fc_w = (rng.standard_normal((2048, num_classes), dtype=np.float32) * np.sqrt(1.0 / 2048)).astype(np.float32)
+    if not onnx_ops:
+        inits["gap_axes"] = np.array([2, 3], np.int64)
+        nodes.append(Node("ReduceMean", [x, "gap_axes"], ["gap"], {"keepdims": 0}))
+        inits["fc.w"] = fc_w
+        inits["fc.b"] = np.zeros(num_classes, np.float32)
+        nodes.append(Node("MatMul", ["gap", "fc.w"], ["fc.mm"]))
+        nodes.append(Node("Add", ["fc.mm", "fc.b"], ["logits"]))
+    else:
+        nodes.append(Node("GlobalAveragePool", [x], ["gap"]))
+        nodes.append(Node("Flatten", ["gap"], ["flat"], {"axis": 1}))
+        inits["fc.weight"] = np.ascontiguousarray(fc_w.T)  # [num_classes, 2048] as torch stores it
+        inits["fc.bias"] = (rng.standard_normal(num_classes, dtype=np.float32) * 0.01).astype(np.float32)
+        nodes.append(Node("Gemm", ["flat", "fc.weight", "fc.bias"], ["logits"],
+                          {"alpha": 1.0, "beta": 1.0, "transB": 1}))
     return GraphDef(nodes, inits, ["data"], ["logits"], opset=18)
 
 

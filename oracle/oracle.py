@@ -379,6 +379,73 @@ _ONNX_DTYPES = {1: np.float32, 6: np.int32, 7: np.int64, 9: np.bool_, 11: np.flo
 
 
 # ----------------------------------------------------------------------------
+# ONNX ops the reference names but does not implement (OpType.cs:17,51,57,58;
+# absent from CPUExecutionProvider.SupportedOps, CPUExecutionProvider.cs:24-50).
+# Restated from the ONNX operator specification, every step a float32 op
+# rounded once, composed from the reference's own kernels where one exists
+# (the GEMM order of MathOps.cs:380-410, ReduceMean = ReduceSum then divide).
+# Parity on these is against the ONNX semantics, not a reference binary.
+# ----------------------------------------------------------------------------
+
+def gemm(a, b, c=None, alpha=1.0, beta=1.0, trans_a=0, trans_b=0):
+    """ONNX Gemm: Y = alpha * op(A) . op(B) + beta * C (C broadcast to [M, N])."""
+    a = _f32(a)
+    b = _f32(b)
+    if a.ndim != 2 or b.ndim != 2:
+        raise OracleError("Gemm inputs must be of rank 2")
+    if trans_a:
+        a = _f32(a.T)
+    if trans_b:
+        b = _f32(b.T)
+    y = matmul(a, b)
+    if alpha != 1.0:
+        y = (np.float32(alpha) * y).astype(np.float32)
+    if c is not None and beta != 0.0:
+        cc = _f32(c)
+        if beta != 1.0:
+            cc = (np.float32(beta) * cc).astype(np.float32)
+        y = binary("Add", y, cc)
+    return y
+
+
+def batch_norm(x, scale, bias, mean, var, epsilon=1e-5):
+    """ONNX BatchNormalization (inference): (x - mean) / sqrt(var + eps) * scale + B
+    over axis 1, each step a float32 operation."""
+    x = _f32(x)
+    shp = (1, -1) + (1,) * (x.ndim - 2)
+    m, v, s, b = (_f32(t).reshape(shp) for t in (mean, var, scale, bias))
+    den = np.sqrt((v + np.float32(epsilon)).astype(np.float32)).astype(np.float32)
+    return ((((x - m).astype(np.float32) / den).astype(np.float32) * s).astype(np.float32) + b).astype(np.float32)
+
+
+def global_average_pool(x):
+    """ONNX GlobalAveragePool: ReduceMean over every spatial axis, kept as 1s."""
+    x = _f32(x)
+    return reduce_mean(x, list(range(2, x.ndim)), 1)
+
+
+def flatten(x, axis=1):
+    x = np.asarray(x)
+    axis = _neg(x.ndim, axis) if axis < 0 else axis
+    outer = int(np.prod(x.shape[:axis])) if axis > 0 else 1
+    return x.reshape(outer, -1 if outer else 0)
+
+
+def slice_(data, starts, ends, axes=None, steps=None):
+    """Slice (CPUExecutionProvider.Slice, CPUExecutionProvider.cs:548-600):
+    numpy slicing with ONNX clamping of starts/ends."""
+    data = np.asarray(data)
+    starts = [int(v) for v in np.asarray(starts).reshape(-1)]
+    ends = [int(v) for v in np.asarray(ends).reshape(-1)]
+    axes = list(range(len(starts))) if axes is None else [int(v) for v in np.asarray(axes).reshape(-1)]
+    steps = [1] * len(starts) if steps is None else [int(v) for v in np.asarray(steps).reshape(-1)]
+    sl = [slice(None)] * data.ndim
+    for s, e, a, st in zip(starts, ends, axes, steps):
+        sl[_neg(data.ndim, a)] = slice(s, e, st)
+    return np.ascontiguousarray(data[tuple(sl)])
+
+
+# ----------------------------------------------------------------------------
 # Graph executor: ComputationalGraph.Execute (ComputationalGraph.cs:199-272)
 # ----------------------------------------------------------------------------
 
@@ -433,11 +500,30 @@ def run_node(node, get, opset=13, honor_conv_attrs=False):
     if op == "Cast":
         return [np.asarray(I(0)).astype(_ONNX_DTYPES[int(a["to"])])]
     if op == "Constant":
-        return [np.asarray(a["value"])]
+        for key in ("value", "value_float", "value_floats", "value_int", "value_ints"):
+            if key in a:
+                v = a[key]
+                dt = np.float32 if key.startswith("value_float") else (np.int64 if key.startswith("value_int") else None)
+                return [np.asarray(v, dt) if dt is not None else np.asarray(v)]
+        raise OracleError("The required attribute value is missing or null.")
     if op == "Shape":
         return [np.array(np.asarray(I(0)).shape, np.int64)]
     if op == "Concat":
         return [np.concatenate([np.asarray(t) for t in ins], axis=a["axis"])]
+    if op == "Slice":
+        return [slice_(I(0), I(1), I(2), I(3), I(4))]
+    if op == "Gemm":
+        return [gemm(I(0), I(1), I(2), a.get("alpha", 1.0), a.get("beta", 1.0), a.get("transA", 0),
+                     a.get("transB", 0))]
+    if op == "BatchNormalization":
+        return [batch_norm(I(0), I(1), I(2), I(3), I(4), a.get("epsilon", 1e-5))]
+    if op == "GlobalAveragePool":
+        return [global_average_pool(I(0))]
+    if op == "Flatten":
+        return [flatten(I(0), a.get("axis", 1))]
+    if op in ("Identity", "Dropout"):
+        x = np.asarray(I(0))
+        return [x, np.ones(x.shape, bool)]
     raise OracleError(f"The operation {op} is not supported by the backend.")
 
 
