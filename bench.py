@@ -1,19 +1,23 @@
-"""Benchmark: e5-small-shaped encoder inference on B200 (BASELINE config 4).
+"""Benchmark: e5-small-shaped encoder inference on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
 
 One step = one forward pass of the 12-layer encoder (hidden 384, 12 heads,
-FFN 1536, vocab 250037, seq 128) over a batch of B = 256 sequences per GPU,
-through the native graph executor (fused GEMM/attention/LayerNorm kernels).
-Multi-GPU is batch sharding with one full replica per GPU and no collective
-("weak" scaling: every rank runs B sequences); torch.distributed (NCCL) is
-used only for the start/stop barrier and the max-over-ranks timing.
+FFN 1536, vocab 250037, seq 128) over a global batch of B = 256 sequences,
+batch-sharded across the N GPUs of the run (256/N contiguous rows per GPU,
+one full graph replica per GPU, no collective on the data path).  Under
+torchrun (N > 1) torch.distributed is used for the start/stop barrier, the
+max-over-ranks timing and, in the end-to-end leg, the host-side gather of
+the pooled embeddings (a gloo group; the device never takes part).
 
-value: sequences/s with inputs already resident in HBM (CUDA events on the
-executor's stream).  e2e: the same through the public API with host numpy
-inputs -- H2D of the int64 ids/mask/type ids and D2H of the pooled
-embeddings inside the timed region.  roofline: the dominant kernel (the
-tensor-core GEMM at the FFN1 shape) timed live on its own.
+value: sequences/s of the whole job (B / the slowest rank's step time) with
+every rank's input slice resident in HBM (CUDA events on the executor's
+stream), "scaling": "strong".  e2e: the same through the public API with
+host numpy inputs -- each step every rank slices the global host batch,
+copies its int64 ids/mask/type ids in, runs, copies its pooled embeddings
+out, and the slices are concatenated on the host in rank order.  weak: the
+extra line item with 256 sequences per GPU.  roofline: the dominant kernel
+(the tensor-core GEMM at the FFN1 shape) timed live on its own.
 
 --impl reference times the reference's CPU algorithm on this host: the
 oracle's C restatement (oracle/, the reference itself is C#/.NET and cannot
@@ -36,7 +40,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 SEQ = 128
-METRIC = "e5-small encoder throughput (batch-sharded replicas)"
+METRIC = "e5-small encoder throughput (global batch 256 sharded across GPUs)"
 UNIT = "seq/s"
 
 
@@ -300,6 +304,46 @@ def cpu_baseline(n_seq=8, g=None):
                       f"({dt:.2f} s); the reference itself is C#/.NET and no .NET runtime exists on this image"}
 
 
+def cpu_baselines_other(gemm_reps=1):
+    """The oracle (1 host thread) on the other workloads the bench line
+    reports: MNIST-8 at batch 1, the four single-op GEMM shapes (transB = 0,
+    alpha = beta = 1, bias), one 224 x 224 ResNet-50 image."""
+    from onnx_b200 import graphs as G
+    from oracle import oracle as O
+    out = {"cores": 1, "kind": "port"}
+    g = G.mnist8(seed=0)
+    x = np.random.default_rng(0).uniform(0, 1, (1, 1, 28, 28)).astype(np.float32)
+    O.execute(g, {"Input3": x})
+    t0 = time.perf_counter()
+    n = 50
+    for _ in range(n):
+        O.execute(g, {"Input3": x})
+    dt = (time.perf_counter() - t0) / n
+    out["mnist8"] = {"us_per_img": round(dt * 1e6, 1), "img_per_s": round(1 / dt, 1),
+                     "sample": f"{n} batch-1 forwards"}
+    rng = np.random.default_rng(7)
+    sweep = []
+    for M, K, N in SWEEP:
+        A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+        Bm = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+        bias = rng.uniform(-1, 1, N).astype(np.float32)
+        reps = max(1, min(20, int(2e9 // (2 * M * N * K)))) if gemm_reps else 1
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            O.binary("Add", O.matmul(A, Bm), bias)
+        dt = (time.perf_counter() - t0) / reps
+        sweep.append({"M": M, "K": K, "N": N, "us": round(dt * 1e6, 1),
+                      "gflops": round(2.0 * M * N * K / dt / 1e9, 2)})
+    out["gemm_sweep"] = sweep
+    g = G.resnet50(seed=0)
+    x = np.random.default_rng(0).uniform(0, 1, (1, 3, 224, 224)).astype(np.float32)
+    t0 = time.perf_counter()
+    O.execute(g, {"data": x}, honor_conv_attrs=True)
+    dt = time.perf_counter() - t0
+    out["resnet50"] = {"ms_per_img": round(dt * 1e3, 1), "img_per_s": round(1 / dt, 3), "sample": "1 image 224^2"}
+    return out
+
+
 def run_reference(args):
     """Reference arm: the reference's CPU algorithm (oracle restatement) on the
     host, rank 0 only; each step is a bounded 4-sequence sample."""
@@ -316,7 +360,7 @@ def run_reference(args):
                     "1 thread; the reference is single-threaded); the reference is C#/.NET and no .NET runtime "
                     "exists on this image"}
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": {"workload": "e5-small-shaped encoder (12 layers, hidden 384, 12 heads, "
                                                         "FFN 1536, vocab 250037), seq 128, mean-pooled"},
             "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -434,7 +478,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--batch", type=int, default=256, help="sequences per GPU")
+    ap.add_argument("--batch", type=int, default=256, help="global batch (sharded across the GPUs)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--vocab", type=int, default=250037)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -495,14 +539,18 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
 
     from onnx_b200 import graphs as G
+    from onnx_b200 import shard
     from onnx_b200.tensor import Context, DeviceTensor
     ctx = Context(local)
     st = torch.cuda.ExternalStream(ctx.stream)
     g, cg = build_graph(ctx, args.vocab)
-    B = args.batch
-    host_inp = G.e5_inputs(B, SEQ, args.vocab, seed=100 + rank)
+    B = args.batch  # global batch, sharded across the ranks
+    lo, hi = shard.shard_bounds(B, world, rank)
+    host_all = G.e5_inputs(B, SEQ, args.vocab, seed=100)
+    host_inp = shard.shard_inputs(host_all, world, rank)
     dev_inp = {k: DeviceTensor.from_host(ctx, v) for k, v in host_inp.items()}
     ctx.sync()
+    gloo = dist.new_group(backend="gloo") if world > 1 else None
 
     def barrier():
         if world > 1:
@@ -515,38 +563,62 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    # ---- device-resident (value) ----
+    def timed_steps(run, steps):
+        """CUDA-event ms per step on the executor's stream, max over ranks."""
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            run()
+        e1.record(st)
+        e1.synchronize()
+        ctx.sync()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
+    # ---- device-resident (value): this rank's slice of the global batch ----
     cg.set_inputs(dev_inp)
     for _ in range(args.warmup):
         cg.run()
     ctx.sync()
-    barrier()
-    torch.cuda.synchronize()
     l0 = ctx.launches
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
-        e0.record(st)
-        for _ in range(args.steps):
-            cg.run()
-        e1.record(st)
-        e1.synchronize()
-    ctx.sync()
+        ms = timed_steps(cg.run, args.steps)
     launches = ctx.launches - l0  # all of this library's launches in the timed region
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     barrier()
 
-    # ---- end to end through the public API (host arrays in, host embeddings out) ----
+    # ---- end to end through the public API: host batch sliced per rank, H2D,
+    # execute, D2H, slices concatenated on the host in rank order ----
+    execute = lambda sl: {"sentence_embedding": cg.execute(sl)["sentence_embedding"]}
+    if world > 1:
+        run_e2e = lambda: shard.run_sharded(execute, host_all, group=gloo)["sentence_embedding"]
+    else:
+        run_e2e = lambda: execute(host_all)["sentence_embedding"]
     for _ in range(args.warmup):
-        cg.execute(host_inp)
+        out = run_e2e()
     barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        out = cg.execute(host_inp)["sentence_embedding"]
+        out = run_e2e()
     ctx.sync()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / args.steps)
-    h2d = sum(v.nbytes for v in host_inp.values())
+    assert out.shape == (B, 384)
+    h2d = sum(v.nbytes for v in host_inp.values()) * world
     d2h = out.nbytes
+
+    # ---- weak scaling (extra): 256 sequences per GPU ----
+    weak = None
+    if world > 1:
+        wk = {k: DeviceTensor.from_host(ctx, v) for k, v in G.e5_inputs(256, SEQ, args.vocab, seed=200 + rank).items()}
+        cg.set_inputs(wk)
+        for _ in range(args.warmup):
+            cg.run()
+        ms_w = timed_steps(cg.run, args.steps)
+        weak = {"batch_per_gpu": 256, "value": round(world * 256 / (ms_w * 1e-3), 2), "unit": UNIT,
+                "ms_per_step": round(ms_w, 3)}
+        del wk
+        cg.set_inputs(dev_inp)
 
     roof = gemm_roofline(ctx, st, torch) if rank == 0 else None
     sweep = gemm_sweep(ctx, st, torch) if rank == 0 else None
@@ -557,22 +629,28 @@ def main():
     clocks = clk.summary()
     if rank == 0:
         cb = None if args.no_cpu_baseline else cpu_baseline(8)
-        value = world * B / (ms * 1e-3)
+        cbo = None if args.no_cpu_baseline or world > 1 else cpu_baselines_other()
+        value = B / (ms * 1e-3)
         line = {"metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "f32 (3xTF32 tensor-core GEMMs, fp32 accumulate)",
                 "data": "synthetic (seeded ids/masks, random-init N(0,0.02) weights)",
                 "config": {"workload": "e5-small-shaped encoder (12 layers, hidden 384, 12 heads, FFN 1536, "
                                        "vocab 250037), seq 128, mean-pooled",
-                           "batch_per_gpu": B, "global_batch": B * world, "seq_len": SEQ,
-                           "parallelism": f"batch-sharded replicas x{world}, no collective",
-                           "l2": "working set per step >> 126 MB L2 (384 MB embedding table, 85 MB layer "
-                                 "weights, 50-200 MB activations); no explicit flush"},
-                "e2e": {"value": round(world * B / (e2e_ms * 1e-3), 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                        "d2h_bytes_per_step": d2h},
-                "gpu_launches": launches * world, "gpu_launches_per_step_per_gpu": launches // args.steps, "roofline": roof, "cpu_baseline": cb, "clocks": clocks,
+                           "global_batch": B, "batch_per_gpu": hi - lo, "seq_len": SEQ,
+                           "parallelism": f"batch-sharded replicas x{world} ({hi - lo} rows each), no collective "
+                                          "on the data path",
+                           "l2": "working set per step >> 126 MB L2 at batch 256 (384 MB embedding table, 85 MB "
+                                 "layer weights, 50-200 MB activations); no explicit flush"},
+                "e2e": {"value": round(B / (e2e_ms * 1e-3), 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h,
+                        "path": "ComputationalGraph.execute per rank on its host slice (+ host gather in rank "
+                                "order when N > 1), wall clock, max over ranks"},
+                "weak": weak,
+                "gpu_launches": launches * world, "gpu_launches_per_step_per_gpu": launches // args.steps,
+                "roofline": roof, "cpu_baseline": cb, "clocks": clocks,
                 "flops_per_seq": G.e5_flops_per_seq(), "e5_batch32": b32, "gemm_sweep": sweep, "mnist": mnist,
-                "resnet50": resnet, "bandwidth_kernels": bw}
+                "resnet50": resnet, "bandwidth_kernels": bw, "cpu_baseline_other_configs": cbo}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
