@@ -137,7 +137,7 @@ SWEEP = [(128, 384, 384), (4096, 384, 1536), (4096, 1536, 384), (8192, 1024, 409
 
 
 def gemm_sweep(ctx, st, torch, reps=10):
-    """BASELINE's single-op Gemm sweep: Y = A.op(B) + bias through the public
+    """The single-op Gemm sweep: Y = A.op(B) + bias through the public
     C-ABI entry point (lonnx_gemm_f32, alpha = beta = 1, bias [N]), A and B
     ~ U[-1, 1], transB in {0, 1}.  Each call includes the per-call tf32
     split of B (the op receives a raw weight).  CUDA events, warm."""
@@ -254,7 +254,7 @@ def bandwidth_kernels(ctx, st, torch, reps=10, scale=1):
 
 
 def e5_batch(ctx, st, torch, cg, vocab, batch=32, reps=10):
-    """the same encoder at batch 32, device-resident inputs."""
+    """The same encoder at batch 32, device-resident inputs."""
     from onnx_b200 import graphs as G
     from onnx_b200.tensor import DeviceTensor
     inp = {k: DeviceTensor.from_host(ctx, v) for k, v in G.e5_inputs(batch, SEQ, vocab, seed=7).items()}
@@ -383,7 +383,7 @@ def profile_case(batch):
 
 
 def mnist_latency(ctx, st, torch, reps=200):
-    """MNIST-8 CNN at batch 1 (BASELINE config 0): device-resident input,
+    """MNIST-8 CNN at batch 1: device-resident input,
     CUDA-event time per forward and the img/s it implies."""
     from onnx_b200 import graphs as G
     from onnx_b200.graph import ComputationalGraph
@@ -417,7 +417,7 @@ def mnist_latency(ctx, st, torch, reps=200):
 
 
 def resnet_throughput(ctx, st, torch, batch=64, reps=5):
-    """ResNet-50 v1 at batch 64 x 3 x 224 x 224 (BASELINE config 3),
+    """ResNet-50 v1 at batch 64 x 3 x 224 x 224,
     device-resident input, img/s over `reps` forwards."""
     from onnx_b200 import graphs as G
     from onnx_b200.graph import ComputationalGraph

@@ -3,7 +3,7 @@
 A ``GraphDef`` mirrors what ``Model.Load`` produces in the reference
 (src/Lokad.Onnx.Backend/Model.cs:30-63): nodes in file order with string
 tensor names and typed attributes, a name -> initializer map, and the graph's
-input/output names.  Two builders produce the BASELINE workloads with seeded
+input/output names.  The builders produce the benchmark workloads with seeded
 synthetic weights:
 
 * ``mnist8``  -- the topology of the reference's test model
@@ -50,7 +50,7 @@ def from_json(path_json: str, arrays: dict, prefix: str = "init/") -> GraphDef:
 
 
 def mnist8(seed: int = 0) -> GraphDef:
-    """mnist-8 topology with N(0, 0.1) weights (BASELINE config 0)."""
+    """mnist-8 topology with N(0, 0.1) weights."""
     rng = np.random.default_rng(seed)
     w = lambda *s: (rng.standard_normal(s) * 0.1).astype(np.float32)
     inits = {
@@ -91,8 +91,8 @@ E5_SMALL = dict(layers=12, hidden=384, heads=12, ffn=1536, vocab=250037, max_pos
 
 def e5_encoder(layers=12, hidden=384, heads=12, ffn=1536, vocab=250037, max_pos=512,
                seq=128, eps=1e-12, seed=0, std=0.02) -> GraphDef:
-    """BERT-style post-LayerNorm encoder shaped like multilingual-e5-small
-    (BASELINE configs 2 and 4), random-init N(0, std) weights.
+    """BERT-style post-LayerNorm encoder shaped like multilingual-e5-small,
+    random-init N(0, std) weights.
 
     Inputs: input_ids, attention_mask, token_type_ids -- int64 [B, seq].
     Output: ``sentence_embedding`` [B, hidden], the attention-mask mean pool
@@ -201,7 +201,7 @@ def e5_encoder(layers=12, hidden=384, heads=12, ffn=1536, vocab=250037, max_pos=
 
 
 def e5_inputs(batch, seq=128, vocab=250037, seed=0):
-    """Synthetic e5 inputs (BASELINE configs 2/4): uniform token ids, an
+    """Synthetic e5 inputs: uniform token ids, an
     attention mask of ones with a random right-padded tail per row (tail
     length uniform in [0, seq-1]), token types all zero."""
     rng = np.random.default_rng(seed + 1)

@@ -1,7 +1,7 @@
 """GEMM / MatMul parity on the GPU, through the C ABI (lonnx_gemm_f32,
 lonnx_matmul_f32), against the oracle's restatement of the reference's
 mm_unsafe_vectorized (src/Lokad.Onnx.Tensors/MathOps.cs:380-410) and, for the
-largest BASELINE shape, against a float64 product (the oracle would take
+largest benchmark shape, against a float64 product (the oracle would take
 minutes there).  Tolerance: |gpu - ref| <= 1e-4 + 1e-4 |ref|."""
 import ctypes
 

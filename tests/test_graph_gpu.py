@@ -81,7 +81,7 @@ def test_mnist8_synthetic_vs_oracle(ctx):
 
 
 def test_resnet50_vs_oracle(ctx):
-    """ResNet-50 v1 (BASELINE config 3) at a small input: strided/padded
+    """ResNet-50 v1 at a small input: strided/padded
     tensor-core convs with fused bias+ReLU, MaxPool, residual Adds, global
     average pool, FC -- against the oracle with Conv attributes applied (the
     reference drops them, so this parity is against the ONNX semantics the
