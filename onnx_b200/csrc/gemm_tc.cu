@@ -48,6 +48,14 @@ constexpr int W_TMA = 0, W_MMA = 1, W_MMA2 = 2, W_A0 = 4, W_ACC0 = 8;
 // kernel modes: plain GEMM (A by TMA, row-major C, one tile per CTA);
 // implicit conv (A gathered, NCHW C, persistent); implicit conv + residual
 constexpr int MODE_GEMM = 0, MODE_CONV = 1, MODE_CONV_RES = 2;
+// K stages per accumulator chunk.  The tensor core accumulates a chunk
+// (CH x 32 K-columns) into TMEM, rounding toward zero; the accumulator warps
+// add chunk sums into fp32 registers with round-to-nearest.  Two 32-wide
+// stages per chunk halve the drains and give the MMAs four stages of slack
+// over an epilogue (two chunk buffers), at a truncation error of a 64-term
+// sum per chunk -- still below the reference's own sequential-fp32 error at
+// the encoder's K.
+constexpr int CH = 2;
 
 // RES: the conv epilogue adds a residual tile, prefetched into shared memory
 // (BM x BN fp32) while the tile's mainloop runs; it costs one ring stage.
@@ -152,6 +160,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                              ? ((int)blockIdx.x < ntiles && nk > 0 ? (ntiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0)
                              : (t0 < ntiles && nk > 0 ? 1 : 0);
     const int total = my_tiles * nk;  // (tile, stage) steps of this CTA
+    // accumulator chunks: CH consecutive K stages of a tile (the last chunk
+    // of a tile may be shorter); one TMEM chunk buffer, one drain per chunk
+    const int nch = (nk + CH - 1) / CH, total_ch = my_tiles * nch;
     auto tile_n0 = [&](int t) { return (t % ntn) * BN; };
     auto tile_m0 = [&](int t) { return (t / ntn) * BM; };
     auto step_tile = [&](int j) { return (int)blockIdx.x + (j / nk) * (int)gridDim.x; };
@@ -245,29 +256,36 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         // the TMA stay within NAB <= S stages of the oldest unfinished MMA.
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_tf32(BM, BN);
-            for (int j = warp - W_MMA; j < total && ok; j += 2) {
-                const int s = j % S, b = j & 1;
-                if (!mbar_wait(conv(s), (j / S) & 1, abort_flag)) { ok = false; break; }
-                // implicit conv: the A warps do not wait for the W tiles, so the MMA does
-                if constexpr (CONV) {
-                    if (!mbar_wait(full(s), (j / S) & 1, abort_flag)) { ok = false; break; }
-                }
-                if (!mbar_wait(tdrain(b), ((j >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                tc_fence_after();
+            // chunk cidx = CH consecutive K stages of one tile, accumulated
+            // by the tensor core into TMEM chunk buffer cidx & 1; issuer
+            // (cidx & 1) owns that buffer, so a chunk's stages are ordered
+            for (int cidx = warp - W_MMA; cidx < total_ch && ok; cidx += 2) {
+                const int tt = cidx / nch, ci = cidx - tt * nch, b = cidx & 1;
+                const int i0 = ci * CH, i1 = min(nk, i0 + CH);
+                if (!mbar_wait(tdrain(b), ((cidx >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
                 const uint32_t acc = tmem + G::ACC_COL + b * BN;
-                const int ab = j % NAB;
-                const uint32_t ahi = tmem + G::A_COL + ab * 64, alo = ahi + 32;
-                const uint32_t w = smem_u32(stageW(s)), wlo = smem_u32(stageWlo(s));
+                for (int i = i0; i < i1 && ok; ++i) {
+                    const int j = tt * nk + i, s = j % S;
+                    if (!mbar_wait(conv(s), (j / S) & 1, abort_flag)) { ok = false; break; }
+                    // implicit conv: the A warps do not wait for the W tiles, so the MMA does
+                    if constexpr (CONV) {
+                        if (!mbar_wait(full(s), (j / S) & 1, abort_flag)) { ok = false; break; }
+                    }
+                    tc_fence_after();
+                    const int ab = j % NAB;
+                    const uint32_t ahi = tmem + G::A_COL + ab * 64, alo = ahi + 32;
+                    const uint32_t w = smem_u32(stageW(s)), wlo = smem_u32(stageWlo(s));
 #pragma unroll
-                for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint64_t dw = smem_desc_sw128(w + kk * 32), dwl = smem_desc_sw128(wlo + kk * 32);
-                    mma_tf32_ts(acc, alo + kk * 8, dw, idesc, kk != 0);
-                    mma_tf32_ts(acc, ahi + kk * 8, dwl, idesc, 1);
-                    mma_tf32_ts(acc, ahi + kk * 8, dw, idesc, 1);
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        const uint64_t dw = smem_desc_sw128(w + kk * 32), dwl = smem_desc_sw128(wlo + kk * 32);
+                        mma_tf32_ts(acc, alo + kk * 8, dw, idesc, (i != i0) || kk != 0);
+                        mma_tf32_ts(acc, ahi + kk * 8, dwl, idesc, 1);
+                        mma_tf32_ts(acc, ahi + kk * 8, dw, idesc, 1);
+                    }
+                    mma_commit(empty(s));
+                    mma_commit(afree(ab));
                 }
-                mma_commit(empty(s));
-                mma_commit(afree(ab));
-                mma_commit(tfull(b));
+                if (ok) mma_commit(tfull(b));
             }
         }
     } else if (agroup >= 0) {
@@ -513,9 +531,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             float acc[64];
 #pragma unroll
             for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
-            for (int i = 0; i < nk && ok; ++i) {
-                const int j = tt * nk + i, b = j & 1;
-                if (!mbar_wait(tfull(b), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+            for (int ci = 0; ci < nch && ok; ++ci) {
+                const int cidx = tt * nch + ci, b = cidx & 1;
+                if (!mbar_wait(tfull(b), (cidx >> 1) & 1, abort_flag)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
