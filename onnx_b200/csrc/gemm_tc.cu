@@ -133,6 +133,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     using G = Cfg<BN, RES>;
     constexpr int S = G::STAGES;
     constexpr int NACC = G::NACC, NAG = G::NAG, NAB = G::NAB;
+    static_assert(S >= CH + 1, "a chunk's first conv(s) wait would alias a ring phase (see CH)");
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * G::STAGE);
