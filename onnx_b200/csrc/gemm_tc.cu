@@ -55,6 +55,16 @@ constexpr int MODE_GEMM = 0, MODE_CONV = 1, MODE_CONV_RES = 2;
 // over an epilogue (two chunk buffers), at a truncation error of a 64-term
 // sum per chunk -- still below the reference's own sequential-fp32 error at
 // the encoder's K.
+//
+// Barrier-phase invariant: the two issuers alternate chunks, so when an
+// issuer starts a chunk at stage j its last wait on a ring slot was for
+// stage j - CH - 1 (or none, for the first chunk of issuer 1 at j = CH).
+// Its wait on conv(j % S) with parity (j / S) & 1 is only meaningful once
+// the slot's previous phase (stage j - S) has completed: a parity wait on a
+// barrier still in that previous phase returns at once (the phase before it
+// has the other parity).  The A warps complete stages in order, so the
+// previous phase is complete whenever j - S <= j - CH - 1, i.e. S >= CH + 1.
+// (CH = 4 with a 3-stage ring broke this and faulted.)
 constexpr int CH = 2;
 
 // RES: the conv epilogue adds a residual tile, prefetched into shared memory
