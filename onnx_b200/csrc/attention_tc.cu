@@ -286,14 +286,19 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
         prefetch_tmap(&tq);
         prefetch_tmap(&tk);
         prefetch_tmap(&tv);
-        mbar_arrive_expect_tx(bar_ld, 3 * TILE);
-        tma_load_2d(smem_u32(sm + OFF_Q), &tq, bar_ld, h * DH, b * S);
-        tma_load_2d(smem_u32(sm + OFF_K), &tk, bar_ld, h * DH, b * S);
-        tma_load_2d(smem_u32(sm + OFF_VTLO), &tv, bar_ld, h * DH, b * S);
     }
     if (warp == 0) {
         tmem_alloc(smem_u32(tmem_slot), 256);
         tmem_relinquish();
+    }
+    // set-up done: wait for the QKV projection (launched with PDL)
+    pdl_wait();
+    pdl_trigger();
+    if (t == 0) {
+        mbar_arrive_expect_tx(bar_ld, 3 * TILE);
+        tma_load_2d(smem_u32(sm + OFF_Q), &tq, bar_ld, h * DH, b * S);
+        tma_load_2d(smem_u32(sm + OFF_K), &tk, bar_ld, h * DH, b * S);
+        tma_load_2d(smem_u32(sm + OFF_VTLO), &tv, bar_ld, h * DH, b * S);
     }
     // the mask in log2 units (scores are exponentiated as 2^(u - u_max) with
     // u = s * log2(e) / scale + mask * log2(e))
@@ -484,10 +489,8 @@ int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v,
             LONNX_CUDA(cudaFuncSetAttribute(k_attention_tc8, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM8));
             attr8_set[ctx->device & 63] = true;
         }
-        k_attention_tc8<<<B * heads, AT8, SMEM8, ctx->stream>>>(mq, mk, mv, mask, out, S, heads, scale,
-                                                                  ctx->dev_flags);
-        LONNX_CHECK_LAUNCH(ctx);
-        return LONNX_OK;
+        return launch_pdl(ctx, k_attention_tc8, dim3(B * heads), dim3(AT8), (size_t)SMEM8, mq, mk, mv, mask, out, S,
+                          heads, scale, ctx->dev_flags);
     }
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {

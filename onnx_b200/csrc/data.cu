@@ -12,6 +12,8 @@ template <typename V>
 __global__ void k_gather_rows(const V *__restrict__ data, int64_t outer, int64_t dim,
                               int64_t inner_v, const int64_t *__restrict__ idx, int64_t n_idx,
                               V *__restrict__ y, int *__restrict__ flags) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t rows = outer * n_idx;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -379,16 +381,15 @@ LONNX_API int lonnx_gather(lonnx_ctx *ctx, const void *data, int elem_bytes, int
     const int64_t row_bytes = inner * elem_bytes;
     const int64_t rows = outer * n_idx;
     const int g = grid_for(ctx, rows * 32);
-    cudaStream_t st = ctx->stream;
     auto al = [](const void *p, int a) { return ((uintptr_t)p % a) == 0; };
     if (row_bytes % 16 == 0 && al(data, 16) && al(y, 16))
-        k_gather_rows<uint4><<<g, 256, 0, st>>>((const uint4 *)data, outer, dim, row_bytes / 16, idx, n_idx, (uint4 *)y, ctx->dev_flags);
-    else if (row_bytes % 4 == 0 && al(data, 4) && al(y, 4))
-        k_gather_rows<uint32_t><<<g, 256, 0, st>>>((const uint32_t *)data, outer, dim, row_bytes / 4, idx, n_idx, (uint32_t *)y, ctx->dev_flags);
-    else
-        k_gather_rows<uint8_t><<<g, 256, 0, st>>>((const uint8_t *)data, outer, dim, row_bytes, idx, n_idx, (uint8_t *)y, ctx->dev_flags);
-    LONNX_CHECK_LAUNCH(ctx);
-    return LONNX_OK;
+        return launch_pdl(ctx, k_gather_rows<uint4>, dim3(g), dim3(256), 0, (const uint4 *)data, outer, dim,
+                          row_bytes / 16, idx, n_idx, (uint4 *)y, ctx->dev_flags);
+    if (row_bytes % 4 == 0 && al(data, 4) && al(y, 4))
+        return launch_pdl(ctx, k_gather_rows<uint32_t>, dim3(g), dim3(256), 0, (const uint32_t *)data, outer, dim,
+                          row_bytes / 4, idx, n_idx, (uint32_t *)y, ctx->dev_flags);
+    return launch_pdl(ctx, k_gather_rows<uint8_t>, dim3(g), dim3(256), 0, (const uint8_t *)data, outer, dim, row_bytes,
+                      idx, n_idx, (uint8_t *)y, ctx->dev_flags);
 }
 
 LONNX_API int lonnx_transpose(lonnx_ctx *ctx, const void *x, int elem_bytes, const int64_t *shape,

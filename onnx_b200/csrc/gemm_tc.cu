@@ -230,6 +230,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // set-up done: wait for the previous kernel's results (launched with PDL)
+    pdl_wait();
+    pdl_trigger();
     bool ok = true;
     const int agroup = (warp >= W_A0 && warp < W_A0 + 4) ? 0 : (NAG == 2 && warp >= G::W_A1 && warp < G::W_A1 + 4) ? 1 : -1;
 
@@ -1033,10 +1036,8 @@ int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, cons
     const int64_t grid = ksplit == 1 ? (tiles > ctx->num_sms ? ctx->num_sms : tiles) : tiles * ksplit;
     // the tail of shared memory holds the conv tap table or the GEMM epilogue staging
     const int smem = MODE != MODE_GEMM ? G::SMEM : G::GEMM_SMEM;
-    k_gemm_tf32x3<BN, MODE><<<(unsigned)grid, kThreads, smem, ctx->stream>>>(ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi,
-                                                                ctx->dev_flags, cv, ksplit, split_stride);
-    LONNX_CHECK_LAUNCH(ctx);
-    return LONNX_OK;
+    return lonnx::launch_pdl(ctx, k_gemm_tf32x3<BN, MODE>, dim3((unsigned)grid), dim3(kThreads), (size_t)smem, ma, mw,
+                             mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, ctx->dev_flags, cv, ksplit, split_stride);
 }
 
 // Split-K finish: C = act(alpha * sum_s ws[s] + beta * bias), the partial

@@ -128,7 +128,43 @@ int gemm_simt(lonnx_ctx *ctx, const float *A, const float *B, const float *bias,
               int batch, int M, int N, int K, int64_t sA, int64_t sB, int64_t sC, int transB,
               float alpha, float beta, int epi, const float *residual);
 
+// Programmatic dependent launch (sm_90+).  A kernel launched by launch_pdl
+// may start while the previous kernel on the stream is still running: its
+// CTAs do their set-up (barrier init, TMEM allocation, tensor-map prefetch)
+// and then pdl_wait(), which returns once the previous kernel has completed
+// and its memory is visible.  No global memory may be read or written
+// before pdl_wait(): the buffers this kernel reads are being produced, and
+// the ones it writes may still be read by the previous kernel.
+// pdl_trigger() lets the next kernel be scheduled once every CTA of this one
+// has started (or exited); without it that happens at this kernel's end.
+// Kernels launched without the attribute see pdl_wait() return at once.
+// LONNX_PDL=0 turns the attribute off (every launch fully serialised).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(lonnx_ctx *ctx, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+    ctx->launches++;
+    if (e != cudaSuccess) return cuda_error(e, "kernel launch");
+    const cudaError_t e2 = cudaGetLastError();
+    if (e2 != cudaSuccess) return cuda_error(e2, "kernel launch");
+    return LONNX_OK;
+}
+
 }  // namespace lonnx
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Numerics shared by kernels -------------------------------------------------
 

@@ -101,6 +101,8 @@ template <int VPT>
 __global__ void k_layernorm(const float *__restrict__ x, const float *__restrict__ res,
                             const float *__restrict__ gamma, const float *__restrict__ beta,
                             float eps, float *__restrict__ y, int64_t rows, int cols) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const float fn = (float)cols;
@@ -144,6 +146,8 @@ __global__ void k_layernorm_block(const float *__restrict__ x, const float *__re
                                   const float *__restrict__ gamma, const float *__restrict__ beta,
                                   float eps, float *__restrict__ y, int64_t rows, int cols) {
     __shared__ float red[32];
+    pdl_wait();
+    pdl_trigger();
     const int64_t r = blockIdx.x;
     if (r >= rows) return;
     const float *xr = x + r * cols;
@@ -333,14 +337,11 @@ LONNX_API int lonnx_layernorm_f32(lonnx_ctx *ctx, const float *x, const float *r
     if (rc) return rc;
     if (!x || !gamma || !beta || !y || rows < 0 || cols <= 0) return set_error(LONNX_E_BADARG, "layernorm: bad arguments");
     if (rows == 0) return LONNX_OK;
-    cudaStream_t st = ctx->stream;
     const int g = grid_for(ctx, rows * 32);
-    if (cols <= 128) k_layernorm<4><<<g, 256, 0, st>>>(x, res, gamma, beta, eps, y, rows, cols);
-    else if (cols <= 384) k_layernorm<12><<<g, 256, 0, st>>>(x, res, gamma, beta, eps, y, rows, cols);
-    else if (cols <= 1024) k_layernorm<32><<<g, 256, 0, st>>>(x, res, gamma, beta, eps, y, rows, cols);
-    else k_layernorm_block<<<(unsigned)rows, 256, 0, st>>>(x, res, gamma, beta, eps, y, rows, cols);
-    LONNX_CHECK_LAUNCH(ctx);
-    return LONNX_OK;
+    if (cols <= 128) return launch_pdl(ctx, k_layernorm<4>, dim3(g), dim3(256), 0, x, res, gamma, beta, eps, y, rows, cols);
+    if (cols <= 384) return launch_pdl(ctx, k_layernorm<12>, dim3(g), dim3(256), 0, x, res, gamma, beta, eps, y, rows, cols);
+    if (cols <= 1024) return launch_pdl(ctx, k_layernorm<32>, dim3(g), dim3(256), 0, x, res, gamma, beta, eps, y, rows, cols);
+    return launch_pdl(ctx, k_layernorm_block, dim3((unsigned)rows), dim3(256), 0, x, res, gamma, beta, eps, y, rows, cols);
 }
 
 LONNX_API int lonnx_reduce_f32(lonnx_ctx *ctx, int op, const float *x, const int64_t *shape,

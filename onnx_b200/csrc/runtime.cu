@@ -8,6 +8,18 @@
 
 namespace lonnx {
 
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("LONNX_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+}  // namespace lonnx
+
+namespace lonnx {
+
 static thread_local std::string g_last_error;
 
 int set_error(int code, const char *fmt, ...) {
