@@ -465,6 +465,321 @@ k_attention_tc8(const __grid_constant__ CUtensorMap tq, const __grid_constant__ 
     }
 }
 
+// ---------------------------------------------------------------------------
+// k_attention_pf: persistent, prefetching version of k_attention_tc8.
+//
+// A CTA (8 warps, two per SM) walks the (sequence, head) pairs b, b + grid,
+// ...  Q and the softmax numerators E live in TMEM as the A operand of the
+// MMAs (tcgen05.mma with A from TMEM), so shared memory holds only K, K_lo,
+// V^T, V^T_lo and two staging tiles for the raw Q and V of the NEXT pair,
+// which one thread loads by TMA while the current pair is being computed
+// (K is reloaded into its slot once the current S = Q K^T is done).
+//
+// TMEM (256 columns): [0, 128) S, overwritten in place by E; [128, 192)
+// Q_hi | Q_lo, later E_lo of the current 64-key half; [192, 224) O_a =
+// E_lo V + E V; [224, 256) O_b = E V_lo (two accumulators, two issuers).
+//
+// Per pair: wait for its loads; Q -> TMEM as tf32 hi / lo, K_lo beside K,
+// V transposed into V^T / V^T_lo; thread 0 starts the next pair's Q / V
+// loads and issues S (12 MMAs); the softmax warps (w and w + 4 share a
+// lane quarter and take keys [32 g, +32) and [64 + 32 g, +32)) read their
+// 64 scores once, meet at the row max, and per 64-key half write E and
+// E_lo into TMEM; two threads issue O += E V per half; the epilogue sums
+// O_a + O_b, divides by the row sum and stores 16 columns per group.
+// The exponent, mask handling and summation order are those of
+// k_attention_tc8.  Every wait is bounded; on expiry the CTA records
+// LONNX_E_TIMEOUT, drains its MMAs and in-flight loads, frees TMEM, returns.
+constexpr int PF_OFF_K = 0, PF_OFF_KLO = TILE, PF_OFF_VT = 2 * TILE, PF_OFF_VTLO = 3 * TILE;
+constexpr int PF_OFF_SQ = 4 * TILE, PF_OFF_SV = 5 * TILE;
+constexpr int PF_OFF_MASK = 6 * TILE;                 // 128 floats
+constexpr int PF_OFF_RED = PF_OFF_MASK + 128 * 4;     // [2][128] max, [2][128] sum
+constexpr int PF_OFF_BAR = PF_OFF_RED + 4 * 128 * 4;  // 6 barriers, TMEM slot, abort flag
+constexpr int PF_SMEM = PF_OFF_BAR + 64 + 1024;
+constexpr uint32_t PF_COL_Q = 128, PF_COL_OA = 192, PF_COL_OB = 224;
+
+// Phase timeline of CTA 0 (clock64 of thread 0), compiled only into a
+// diagnostic build (-DLONNX_ATTN_TIMELINE); read back with
+// lonnx_debug_attention_timeline.
+#ifdef LONNX_ATTN_TIMELINE
+__device__ long long g_attn_tl[256];
+#define ATL(i)                                                            \
+    do {                                                                  \
+        if (blockIdx.x == 0 && t == 0 && it < 8) g_attn_tl[it * 16 + (i)] = clock64(); \
+    } while (0)
+#else
+#define ATL(i) \
+    do {       \
+    } while (0)
+#endif
+
+__global__ void __launch_bounds__(AT8, 2)
+k_attention_pf(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+               const __grid_constant__ CUtensorMap tv, const float *__restrict__ maskadd, float *__restrict__ out,
+               int npairs, int S, int heads, float scale, int *dev_flags) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + PF_OFF_BAR);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 6);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *msk = reinterpret_cast<float *>(sm + PF_OFF_MASK);
+    float *red_max = reinterpret_cast<float *>(sm + PF_OFF_RED), *red_sum = red_max + 2 * 128;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    const uint32_t bar_qv = smem_u32(bars), bar_k = smem_u32(bars + 1), bar_s = smem_u32(bars + 2),
+                   bar_o = smem_u32(bars + 3), bar_drain = smem_u32(bars + 4);
+    const int g = warp >> 2, row = (warp & 3) * 32 + lane;  // row == t & 127
+
+    if (t == 0) {
+        mbar_init(bar_qv, 1);
+        mbar_init(bar_k, 1);
+        mbar_init(bar_s, 1);
+        mbar_init(bar_o, 2);      // one commit per P.V issuer
+        mbar_init(bar_drain, 2);  // the two MMA-issuing threads
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tq);
+        prefetch_tmap(&tk);
+        prefetch_tmap(&tv);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), 256);
+        tmem_relinquish();
+    }
+    // set-up done: wait for the QKV projection (launched with PDL)
+    pdl_wait();
+    pdl_trigger();
+    int pend_qv = 0, pend_k = 0;  // thread 0: loads in flight (for the abort drain)
+    auto load_qv = [&](int pr) {
+        const int b = pr / heads, h = pr - (pr / heads) * heads;
+        mbar_arrive_expect_tx(bar_qv, 2 * TILE);
+        tma_load_2d(smem_u32(sm + PF_OFF_SQ), &tq, bar_qv, h * DH, b * S);
+        tma_load_2d(smem_u32(sm + PF_OFF_SV), &tv, bar_qv, h * DH, b * S);
+        ++pend_qv;
+    };
+    auto load_k = [&](int pr) {
+        const int b = pr / heads, h = pr - (pr / heads) * heads;
+        mbar_arrive_expect_tx(bar_k, TILE);
+        tma_load_2d(smem_u32(sm + PF_OFF_K), &tk, bar_k, h * DH, b * S);
+        ++pend_k;
+    };
+    int pair = blockIdx.x;
+    if (t == 0 && pair < npairs) {
+        load_qv(pair);
+        load_k(pair);
+    }
+    float mreg = 0.0f;  // this thread's mask entry (threads < 128) of the pair being loaded
+    if (t < 128 && maskadd && pair < npairs && t < S) mreg = maskadd[(int64_t)(pair / heads) * S + t];
+    __syncthreads();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const float c2 = kLog2e / scale;
+    bool ok = true;
+
+    for (int it = 0; pair < npairs; ++it, pair += gridDim.x) {
+        const int b = pair / heads, h = pair - b * heads;
+        const int nxt = pair + (int)gridDim.x;
+        const bool has_next = nxt < npairs;
+        ATL(0);
+        // ---- 0. mask (log2 units) of this pair; start loading the next one's
+        if (t < 128) {
+            msk[t] = mreg * kLog2e;
+            mreg = 0.0f;
+            if (maskadd && has_next && t < S) mreg = maskadd[(int64_t)(nxt / heads) * S + t];
+        }
+        // ---- 1. operands: Q -> TMEM (hi | lo), K_lo, V^T / V^T_lo -------------
+        if (ok && !(mbar_wait(bar_qv, it & 1, abort_flag) && mbar_wait(bar_k, it & 1, abort_flag))) ok = false;
+        ATL(1);
+        if (ok) {
+            const int c0 = g * 4;  // this thread: chunks 4g .. 4g + 3 of its row (16 of the 32 columns)
+            uint32_t qh[16], ql[16];
+            float4 vr[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int o = swz(row, c0 + c);
+                const float4 qv = *reinterpret_cast<const float4 *>(sm + PF_OFF_SQ + o);
+                const float q4[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float hv = tf32_hi(q4[u]);
+                    qh[c * 4 + u] = __float_as_uint(hv);
+                    ql[c * 4 + u] = __float_as_uint(__fsub_rn(q4[u], hv));
+                }
+                *reinterpret_cast<float4 *>(sm + PF_OFF_KLO + o) =
+                    lo4(*reinterpret_cast<const float4 *>(sm + PF_OFF_K + o));
+                vr[c] = *reinterpret_cast<const float4 *>(sm + PF_OFF_SV + o);
+            }
+            tmem_st_32x32b_x16(lane_addr + PF_COL_Q + g * 16, qh);
+            tmem_st_32x32b_x16(lane_addr + PF_COL_Q + 32 + g * 16, ql);
+            const bool live = row < S;
+            const int atom = row >> 5, ch = (row & 31) >> 2, wd = row & 3;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const float e4[4] = {vr[c].x, vr[c].y, vr[c].z, vr[c].w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int d = (c0 + c) * 4 + u;
+                    const int off = atom * 32 * ROWB + swz(d, ch) + wd * 4;
+                    const float x = live ? e4[u] : 0.0f;
+                    *reinterpret_cast<float *>(sm + PF_OFF_VT + off) = x;
+                    *reinterpret_cast<float *>(sm + PF_OFF_VTLO + off) = __fsub_rn(x, tf32_hi(x));
+                }
+            }
+            tmem_st_wait();
+        }
+        if (!ok) *abort_flag = 1;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+        ok = ok && !*abort_flag;
+        ATL(2);
+
+        // ---- 2. next pair's Q / V into the staging tiles; S = Q K^T --------------
+        if (t == 0 && ok) {
+            if (has_next) load_qv(nxt);
+            constexpr uint32_t idesc = idesc_tf32(128, 128);
+            const uint32_t bk = smem_u32(sm + PF_OFF_K), bl = smem_u32(sm + PF_OFF_KLO);
+            const uint32_t qhi = tmem + PF_COL_Q, qlo = tmem + PF_COL_Q + 32;
+#pragma unroll
+            for (int kk = 0; kk < DH / 8; ++kk) {
+                const uint32_t ko = kk * 32;
+                mma_tf32_ts(tmem, qlo + kk * 8, smem_desc_sw128(bk + ko), idesc, kk != 0);
+                mma_tf32_ts(tmem, qhi + kk * 8, smem_desc_sw128(bl + ko), idesc, 1);
+                mma_tf32_ts(tmem, qhi + kk * 8, smem_desc_sw128(bk + ko), idesc, 1);
+            }
+            mma_commit(bar_s);
+        }
+        ATL(3);
+        if (ok && !mbar_wait(bar_s, it & 1, abort_flag)) ok = false;
+        tc_fence_after();
+        ATL(4);
+        if (t == 0 && ok && has_next) load_k(nxt);  // K / K_lo are no longer read
+
+        // ---- 3. scores: this thread's 64 keys, read once -------------------------
+        uint32_t r0[32], r1[32];
+        float mx = 0.0f;  // the reference's running max starts at 0; 0 maps to 0 in log2 units
+        if (ok) {
+            tmem_ld_32x32b_x32(lane_addr + g * 32, r0);
+            tmem_ld_32x32b_x32(lane_addr + 64 + g * 32, r1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int k0 = g * 32 + j, k1 = 64 + g * 32 + j;
+                if (k0 < S) mx = fmaxf(mx, fmaf(__uint_as_float(r0[j]), c2, msk[k0]));
+                if (k1 < S) mx = fmaxf(mx, fmaf(__uint_as_float(r1[j]), c2, msk[k1]));
+            }
+        }
+        red_max[g * 128 + row] = mx;
+        if (!ok) *abort_flag = 1;
+        __syncthreads();
+        ok = ok && !*abort_flag;
+        ATL(5);
+        mx = fmaxf(red_max[row], red_max[128 + row]);
+
+        // ---- 4. two 64-key halves: E, E_lo -> TMEM, O += E V ---------------------
+        float sum = 0.0f;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+            if (ok) {
+                const uint32_t(&r)[32] = hf ? r1 : r0;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {  // 16 keys at a time (register pressure)
+                    uint32_t eh[16], el[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int key = hf * 64 + g * 32 + q * 16 + j;
+                        const float e =
+                            key < S ? ex2_approx(fmaf(__uint_as_float(r[q * 16 + j]), c2, msk[key]) - mx) : 0.0f;
+                        sum += e;
+                        eh[j] = __float_as_uint(e);
+                        el[j] = __float_as_uint(__fsub_rn(e, tf32_hi(e)));
+                    }
+                    tmem_st_32x32b_x16(lane_addr + hf * 64 + g * 32 + q * 16, eh);  // E over its own scores
+                    tmem_st_32x32b_x16(lane_addr + PF_COL_Q + g * 32 + q * 16, el);
+                }
+                tmem_st_wait();
+            }
+            if (hf == 1) red_sum[g * 128 + row] = sum;
+            if (!ok) *abort_flag = 1;
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            ok = ok && !*abort_flag;
+            ATL(6 + 3 * hf);
+            if ((t == 0 || t == 32) && ok) {
+                constexpr uint32_t idesc = idesc_tf32(128, DH);
+                const uint32_t oacc = tmem + (t == 0 ? PF_COL_OA : PF_COL_OB);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t vatom = hf * 2 + (kk >> 2), ko = (kk & 3) * 32;
+                    const uint32_t ehi = tmem + hf * 64 + kk * 8, elo = tmem + PF_COL_Q + kk * 8;
+                    const uint32_t bv = smem_u32(sm + PF_OFF_VT + vatom * 32 * ROWB) + ko;
+                    const uint32_t bvl = smem_u32(sm + PF_OFF_VTLO + vatom * 32 * ROWB) + ko;
+                    if (t == 0) {
+                        mma_tf32_ts(oacc, ehi, smem_desc_sw128(bv), idesc, (hf | kk) != 0);
+                        mma_tf32_ts(oacc, elo, smem_desc_sw128(bv), idesc, 1);
+                    } else {
+                        mma_tf32_ts(oacc, ehi, smem_desc_sw128(bvl), idesc, (hf | kk) != 0);
+                    }
+                }
+                mma_commit(bar_o);
+            }
+            ATL(7 + 3 * hf);
+            // the next half's E_lo overwrites this half's (and the next pair
+            // reuses V^T) only after these MMAs are done
+            if (ok && !mbar_wait(bar_o, hf, abort_flag)) ok = false;
+            tc_fence_after();
+            ATL(8 + 3 * hf);
+        }
+
+        // ---- 5. O / row sum: group g stores columns [16 g, 16 g + 16) -----------
+        if (ok) {
+            uint32_t oa[16], ob[16];
+            tmem_ld_32x32b_x16(lane_addr + PF_COL_OA + g * 16, oa);
+            tmem_ld_32x32b_x16(lane_addr + PF_COL_OB + g * 16, ob);
+            tmem_ld_wait();
+            if (row < S) {
+                const float inv = 1.0f / (red_sum[row] + red_sum[128 + row]);
+                float *op = out + ((int64_t)b * S + row) * ((int64_t)heads * DH) + (int64_t)h * DH + g * 16;
+#pragma unroll
+                for (int d = 0; d < 16; d += 4) {
+                    float v4[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        v4[u] = __fadd_rn(__uint_as_float(oa[d + u]), __uint_as_float(ob[d + u])) * inv;
+                    *reinterpret_cast<float4 *>(op + d) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+                }
+            }
+        }
+        ATL(12);
+        if (!ok) *abort_flag = 1;
+        tc_fence_before();
+        __syncthreads();  // red, msk and TMEM are reused by the next pair
+        tc_fence_after();
+        ok = ok && !*abort_flag;
+        if (!ok) break;
+    }
+
+    if (!ok) {
+        // drain: MMAs issued by the two issuing threads, TMA loads in flight
+        if (t == 0) atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
+        if (t == 0 || t == 32) {
+            mma_commit(bar_drain);
+            mbar_wait(bar_drain, 0, nullptr, 400000000ll);
+        }
+        if (t == 0) {
+            // the (pend - 1)-th completion of each load barrier is the last one issued
+            if (pend_qv) mbar_wait(bar_qv, (pend_qv - 1) & 1, nullptr, 400000000ll);
+            if (pend_k) mbar_wait(bar_k, (pend_k - 1) & 1, nullptr, 400000000ll);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
 }  // namespace
 
 namespace lonnx {
@@ -484,6 +799,18 @@ int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v,
         if (!rc) rc = make_tile_map_f32(&mk, k, rows, cols, ld, 128);
         if (!rc) rc = make_tile_map_f32(&mv, v, rows, cols, ld, 128);
         if (rc) return rc;
+        static const bool tc8 = getenv("LONNX_ATTN_TC8") != nullptr;
+        if (!tc8) {
+            static bool attr_pf_set[64] = {false};
+            if (!attr_pf_set[ctx->device & 63]) {
+                LONNX_CUDA(cudaFuncSetAttribute(k_attention_pf, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM));
+                attr_pf_set[ctx->device & 63] = true;
+            }
+            const int npairs = B * heads;
+            const int grid = npairs < 2 * ctx->num_sms ? npairs : 2 * ctx->num_sms;  // two CTAs per SM
+            return launch_pdl(ctx, k_attention_pf, dim3(grid), dim3(AT8), (size_t)PF_SMEM, mq, mk, mv, mask, out,
+                              npairs, S, heads, scale, ctx->dev_flags);
+        }
         static bool attr8_set[64] = {false};
         if (!attr8_set[ctx->device & 63]) {
             LONNX_CUDA(cudaFuncSetAttribute(k_attention_tc8, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM8));
@@ -503,3 +830,10 @@ int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v,
 }
 
 }  // namespace lonnx
+
+#ifdef LONNX_ATTN_TIMELINE
+extern "C" LONNX_API int lonnx_debug_attention_timeline(long long *host, int n) {
+    LONNX_CUDA(cudaMemcpyFromSymbol(host, g_attn_tl, sizeof(long long) * (n < 256 ? n : 256)));
+    return LONNX_OK;
+}
+#endif
