@@ -1005,7 +1005,37 @@ EncodeTiledFn get_encode() {
 }
 
 // row-major [rows, cols] fp32 with leading dimension ld; box = box_rows x 32
+int encode_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows);
+
+// Encoded maps are cached per host thread (a map is a pure function of its
+// arguments): encoding costs the host more than a small GEMM runs on the
+// device, and the graph executor calls with the same buffers every step.
 int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+    struct Entry {
+        const float *base;
+        int64_t rows, cols, ld;
+        int box;
+        CUtensorMap map;
+    };
+    constexpr int kEntries = 64;
+    static thread_local Entry cache[kEntries];
+    static thread_local int next = 0;
+    for (int i = 0; i < kEntries; ++i) {
+        const Entry &e = cache[i];
+        if (e.base == base && e.rows == rows && e.cols == cols && e.ld == ld && e.box == box_rows && base) {
+            *map = e.map;
+            return LONNX_OK;
+        }
+    }
+    const int rc = encode_map(map, base, rows, cols, ld, box_rows);
+    if (rc == LONNX_OK) {
+        cache[next] = Entry{base, rows, cols, ld, box_rows, *map};
+        next = (next + 1) % kEntries;
+    }
+    return rc;
+}
+
+int encode_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return lonnx::set_error(LONNX_E_CUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -1151,7 +1181,8 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
     const int64_t tiles = (int64_t)((N + bn - 1) / bn) * ((M + BM - 1) / BM);
     const int nk = (K + BK - 1) / BK;
     int ksplit = 1;
-    if (split_k && allow_scratch && tiles * 2 <= ctx->num_sms) {
+    // (a problem this small is bound by its launches: one kernel, no split)
+    if (split_k && allow_scratch && tiles * 2 <= ctx->num_sms && (int64_t)M * N * K >= ((int64_t)1 << 26)) {
         ksplit = (int)(ctx->num_sms / tiles);
         ksplit = std::min(ksplit, std::min(nk / 3, 16));
         if (ksplit > 1) ksplit = std::min(ksplit, nk);  // every split gets at least one stage
