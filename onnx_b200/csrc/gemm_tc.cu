@@ -30,6 +30,7 @@
 #include <stdio.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <mutex>
 
 #include "lonnx_internal.cuh"
@@ -67,6 +68,25 @@ constexpr int MODE_GEMM = 0, MODE_CONV = 1, MODE_CONV_RES = 2;
 // (CH = 4 with a 3-stage ring broke this and faulted.)
 constexpr int CH = 2;
 
+// Role timeline of CTA 0 (clock64), compiled only into a diagnostic build
+// (-DLONNX_GEMM_TIMELINE); read back with lonnx_debug_gemm_timeline.
+// [0, 256): issuer start of chunk c, [256, 512): issuer commit of chunk c,
+// [512, 768): accumulator warp 8 past tfull of chunk c, [768, 1024): its
+// tdrain arrive, [1024, 1040): epilogue start of tile t, [1040, 1056): end,
+// [1056, 1184): 8 marks inside the epilogue of tile t (t < 16).
+#ifdef LONNX_GEMM_TIMELINE
+__device__ long long g_gemm_tl[1184];
+#define GTL(off, idx)                                                                      \
+    do {                                                                                   \
+        if (blockIdx.x == 0 && (idx) < ((off) >= 1056 ? 128 : (off) >= 1024 ? 16 : 256)) \
+            g_gemm_tl[(off) + (idx)] = clock64();                                          \
+    } while (0)
+#else
+#define GTL(off, idx) \
+    do {              \
+    } while (0)
+#endif
+
 // RES: the conv epilogue adds a residual tile, prefetched into shared memory
 // (BM x BN fp32) while the tile's mainloop runs; it costs one ring stage.
 template <int BN, bool RES = false>
@@ -83,10 +103,12 @@ struct Cfg {
     static constexpr int TAB_MAX = (SMEM - 1024 - TAB_OFF) / 4;  // tap-table entries
     static constexpr int GROUPS = BN / 64;              // accumulator column groups of 64
     static constexpr int NACC = 4 * GROUPS;             // accumulator warps 8 .. 8 + NACC - 1
-    // GEMM epilogue: one 32 x 16 staging block per accumulator warp at TAB_OFF
-    // (16-byte rows of 20 floats: conflict-free float4 writes)
-    static constexpr int STG_PITCH = 20;
-    static constexpr int GEMM_SMEM = TAB_OFF + NACC * 32 * STG_PITCH * 4 + 1024;
+    // GEMM epilogue: one dense 32 x 16 staging block per accumulator warp
+    // (2 KB, 1024-aligned), its 16-byte chunks swizzled as TMA's 64-byte
+    // swizzle lays them out: chunk c of row r at c ^ ((r >> 1) & 3), so the
+    // block is both a TMA store source and conflict-free for float4 access
+    static constexpr int STG_OFF = (TAB_OFF + 1023) & ~1023;
+    static constexpr int GEMM_SMEM = STG_OFF + NACC * 2048 + 1024;
     // A warpgroups: warps 4-7, plus warps 8 + NACC .. +3 when the
     // accumulators leave four warps idle (BN <= 128); each group then moves
     // 16 of a stage's 32 K-columns
@@ -136,9 +158,10 @@ __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__flo
 template <int BN, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
 k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-              const __grid_constant__ CUtensorMap tmWlo, const float *__restrict__ bias, float *__restrict__ C,
-              int M, int N, int K, int ldc, float alpha, float beta, int epi, int *dev_flags,
-              const lonnx::ConvArgs cv, int ksplit, int64_t split_stride) {
+              const __grid_constant__ CUtensorMap tmWlo, const __grid_constant__ CUtensorMap tmC,
+              const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, int ldc, float alpha,
+              float beta, int epi, int *dev_flags, const lonnx::ConvArgs cv, int ksplit, int64_t split_stride,
+              int cstore) {
     constexpr bool CONV = MODE != MODE_GEMM, RES = MODE == MODE_CONV_RES;
     using G = Cfg<BN, RES>;
     constexpr int S = G::STAGES;
@@ -277,6 +300,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 const int tt = cidx / nch, ci = cidx - tt * nch, b = cidx & 1;
                 const int i0 = ci * CH, i1 = min(nk, i0 + CH);
                 if (!mbar_wait(tdrain(b), ((cidx >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                GTL(0, cidx);
                 const uint32_t acc = tmem + G::ACC_COL + b * BN;
                 for (int i = i0; i < i1 && ok; ++i) {
                     const int j = tt * nk + i, s = j % S;
@@ -300,6 +324,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                     mma_commit(afree(ab));
                 }
                 if (ok) mma_commit(tfull(b));
+                GTL(256, cidx);
             }
         }
     } else if (agroup >= 0) {
@@ -548,6 +573,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             for (int ci = 0; ci < nch && ok; ++ci) {
                 const int cidx = tt * nch + ci, b = cidx & 1;
                 if (!mbar_wait(tfull(b), (cidx >> 1) & 1, abort_flag)) { ok = false; break; }
+                if (warp == W_ACC0 && lane == 0) GTL(512, cidx);
                 tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -560,6 +586,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(tdrain(b));
+                if (warp == W_ACC0 && lane == 0) GTL(768, cidx);
             }
             if (!ok) break;
             if constexpr (CONV) {
@@ -610,6 +637,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 }
                 continue;
             }
+            if (warp == W_ACC0 && lane == 0) GTL(1024, tt);
             // row-major epilogue, overlapping the next tile's loads and MMAs:
             // each warp moves its 32 rows x 64 columns out 16 columns at a
             // time through a private 32 x 16 staging block in shared memory
@@ -625,25 +653,33 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 if (bias && col < N) bv = beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col));
                 sb[c] = bv;
             }
+            if (warp == W_ACC0 && lane == 0) GTL(1056, tt * 8);
             asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
-            float *stg = reinterpret_cast<float *>(smem + G::TAB_OFF) + (warp - W_ACC0) * (32 * G::STG_PITCH);
+            if (warp == W_ACC0 && lane == 0) GTL(1056, tt * 8 + 1);
+            // 32 x 16 staging block of this warp; cstore: the finished block
+            // leaves by TMA store (tmC, 64-byte swizzle) instead of st.global
+            float *stg = reinterpret_cast<float *>(smem + G::STG_OFF) + (warp - W_ACC0) * 512;
+            auto sidx = [](int r, int c4) { return r * 16 + ((c4 ^ ((r >> 1) & 3)) << 2); };
             const int rbase = m0 + q * 32, cbase = n0 + grp * 64;
             const float *sbg = sb + grp * 64;
             const bool vec = (ldc & 3) == 0 && (N & 3) == 0 && ((uintptr_t)C & 15) == 0;
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
+                if (warp == W_ACC0 && lane == 0) GTL(1056, tt * 8 + 2 + ch);
+                if (cstore && lane == 0) bulk_wait_group_read0();  // the previous block has left
                 __syncwarp();
 #pragma unroll
-                for (int u = 0; u < 16; u += 4)
-                    *reinterpret_cast<float4 *>(stg + lane * G::STG_PITCH + u) =
-                        make_float4(acc[ch * 16 + u], acc[ch * 16 + u + 1], acc[ch * 16 + u + 2], acc[ch * 16 + u + 3]);
+                for (int u = 0; u < 4; ++u)
+                    *reinterpret_cast<float4 *>(stg + sidx(lane, u)) = make_float4(
+                        acc[ch * 16 + 4 * u], acc[ch * 16 + 4 * u + 1], acc[ch * 16 + 4 * u + 2], acc[ch * 16 + 4 * u + 3]);
                 __syncwarp();
                 // float4 e4 = lane + 32 i of the 32 x 16 block: row e4 / 4, columns 4 (e4 % 4) ..
 #pragma unroll 1
                 for (int i = 0; i < 4; ++i) {
-                    const int e4 = lane + 32 * i, rr = e4 >> 2, c4 = (e4 & 3) * 4;
+                    const int e4 = lane + 32 * i, rr = e4 >> 2, c4i = e4 & 3, c4 = c4i * 4;
                     const int grow = rbase + rr, col0 = cbase + ch * 16 + c4;
-                    const float4 raw = *reinterpret_cast<const float4 *>(stg + rr * G::STG_PITCH + c4);
+                    float *sp = stg + sidx(rr, c4i);
+                    const float4 raw = *reinterpret_cast<const float4 *>(sp);
                     float v[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
@@ -654,6 +690,10 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                         else if (epi == LONNX_EPI_GELU_ERF) x = lonnx_gelu_fast(x);
                         v[u] = x;
                     }
+                    if (cstore) {
+                        *reinterpret_cast<float4 *>(sp) = make_float4(v[0], v[1], v[2], v[3]);
+                        continue;
+                    }
                     if (grow >= M) continue;
                     float *dst = C + (int64_t)grow * ldc + col0;
                     if (vec && col0 + 3 < N) {
@@ -663,8 +703,18 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                             if (col0 + u < N) dst[u] = v[u];
                     }
                 }
+                if (cstore) {
+                    fence_proxy_async_smem();  // the block's generic writes, visible to the TMA unit
+                    __syncwarp();
+                    if (lane == 0 && cbase + ch * 16 < N) {
+                        tma_store_2d(&tmC, smem_u32(stg), cbase + ch * 16, rbase);
+                        bulk_commit_group();
+                    }
+                }
             }
+            if (warp == W_ACC0 && lane == 0) GTL(1040, tt);
         }
+        if (cstore && lane == 0) bulk_wait_group0();  // every block stored before the CTA exits
     }
 
     if (!ok) {
@@ -1005,16 +1055,20 @@ EncodeTiledFn get_encode() {
 }
 
 // row-major [rows, cols] fp32 with leading dimension ld; box = box_rows x 32
-int encode_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows);
+int encode_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+               int kind);
 
 // Encoded maps are cached per host thread (a map is a pure function of its
 // arguments): encoding costs the host more than a small GEMM runs on the
 // device, and the graph executor calls with the same buffers every step.
-int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// kind 0: operand loads, box 32 columns x box_rows, 128-byte swizzle;
+// kind 1: epilogue stores, box 16 columns x box_rows, 64-byte swizzle.
+int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+             int kind = 0) {
     struct Entry {
         const float *base;
         int64_t rows, cols, ld;
-        int box;
+        int box, kind;
         CUtensorMap map;
     };
     constexpr int kEntries = 64;
@@ -1022,37 +1076,57 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
     static thread_local int next = 0;
     for (int i = 0; i < kEntries; ++i) {
         const Entry &e = cache[i];
-        if (e.base == base && e.rows == rows && e.cols == cols && e.ld == ld && e.box == box_rows && base) {
+        if (e.base == base && e.rows == rows && e.cols == cols && e.ld == ld && e.box == box_rows && e.kind == kind &&
+            base) {
             *map = e.map;
             return LONNX_OK;
         }
     }
-    const int rc = encode_map(map, base, rows, cols, ld, box_rows);
+    const int rc = encode_map(map, base, rows, cols, ld, box_rows, kind);
     if (rc == LONNX_OK) {
-        cache[next] = Entry{base, rows, cols, ld, box_rows, *map};
+        cache[next] = Entry{base, rows, cols, ld, box_rows, kind, *map};
         next = (next + 1) % kEntries;
     }
     return rc;
 }
 
-int encode_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+int encode_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+               int kind) {
     EncodeTiledFn enc = get_encode();
     if (!enc) return lonnx::set_error(LONNX_E_CUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t box[2] = {(cuuint32_t)(kind ? 16 : BK), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, kind ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return lonnx::set_error(LONNX_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return LONNX_OK;
+}
+
+// The epilogue stores C by TMA when C can be described by a tensor map
+// (16-byte aligned, ldc a multiple of 4) and K is not split;
+// LONNX_GEMM_TMA_STORE=0 keeps the per-thread global stores.
+bool tma_store_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("LONNX_GEMM_TMA_STORE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 template <int BN, int MODE>
 int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, const CUtensorMap &mwlo,
               const float *bias, float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi,
               const lonnx::ConvArgs &cv, int ksplit = 1, int64_t split_stride = 0) {
+    CUtensorMap mc = mw;  // unused unless cstore
+    int cstore = 0;
+    if (MODE == MODE_GEMM && ksplit == 1 && tma_store_enabled() && (ldc & 3) == 0 && ((uintptr_t)C & 15) == 0) {
+        const int rc = make_map(&mc, C, M, N, ldc, 32, 1);
+        if (rc) return rc;
+        cstore = 1;
+    }
     using G = Cfg<BN, MODE == MODE_CONV_RES>;
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {
@@ -1067,7 +1141,8 @@ int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, cons
     // the tail of shared memory holds the conv tap table or the GEMM epilogue staging
     const int smem = MODE != MODE_GEMM ? G::SMEM : G::GEMM_SMEM;
     return lonnx::launch_pdl(ctx, k_gemm_tf32x3<BN, MODE>, dim3((unsigned)grid), dim3(kThreads), (size_t)smem, ma, mw,
-                             mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, ctx->dev_flags, cv, ksplit, split_stride);
+                             mwlo, mc, bias, C, M, N, K, ldc, alpha, beta, epi, ctx->dev_flags, cv, ksplit,
+                             split_stride, cstore);
 }
 
 // Split-K finish: C = act(alpha * sum_s ws[s] + beta * bias), the partial
@@ -1267,3 +1342,9 @@ int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, i
 
 }  // namespace lonnx
 
+#ifdef LONNX_GEMM_TIMELINE
+extern "C" LONNX_API int lonnx_debug_gemm_timeline(long long *host, int n) {
+    LONNX_CUDA(cudaMemcpyFromSymbol(host, g_gemm_tl, sizeof(long long) * (n < 1184 ? n : 1184)));
+    return LONNX_OK;
+}
+#endif
