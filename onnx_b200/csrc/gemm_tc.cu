@@ -1193,22 +1193,23 @@ bool pair_enabled() {
     return on;
 }
 
-// Tile width for N: 192 or 128, whichever divides N, else the one with the
-// least padding.
+// Tile width for N: 192 or 128, by a cost model of the persistent launch:
+// rounds of tiles over the SMs times the relative time of one tile.  A
+// 128-wide tile takes ~0.77 of a 192-wide one (its stages are MMA-issue
+// bound; measured with the widths forced on the encoder at batch 256:
+// 11.2 vs 10.1 ms per step), so the narrower tile wins only when it does not
+// add a round: e.g. N = 384 at M = 4096 (96 tiles vs 64, one round each),
+// but not at M = 8192 (192 tiles = 2 rounds vs 128 tiles = 1).  The width
+// does not change any output element's summation order.
 int pick_bn(int M, int N, int sms) {
     static const int forced = [] {
         const char *e = getenv("LONNX_GEMM_BN");
         return e ? atoi(e) : 0;
     }();
     if (forced == 128 || forced == 192) return forced;
-    int bn;
-    if (N % 192 == 0) bn = 192;
-    else if (N % 128 == 0) bn = 128;
-    else bn = ((N + 191) / 192 * 192 - N) < ((N + 127) / 128 * 128 - N) ? 192 : 128;
-    // fewer 192-wide tiles than SMs: 128-wide tiles spread the work over
-    // more SMs (each output element is summed in the same order either way)
-    if (bn == 192 && (int64_t)((M + BM - 1) / BM) * ((N + 191) / 192) < sms) bn = 128;
-    return bn;
+    const int64_t rows = (M + BM - 1) / BM;
+    auto rounds = [&](int bn) { return (rows * ((N + bn - 1) / bn) + sms - 1) / sms; };
+    return 0.77 * (double)rounds(128) < (double)rounds(192) ? 128 : 192;
 }
 
 // Conv tile width: the least padding of M among 128, 192 and 64 (ties to
