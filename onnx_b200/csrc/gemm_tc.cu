@@ -668,6 +668,33 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 if (warp == W_ACC0 && lane == 0) GTL(1056, tt * 8 + 2 + ch);
                 if (cstore && lane == 0) bulk_wait_group_read0();  // the previous block has left
                 __syncwarp();
+                if (cstore && epi != LONNX_EPI_GELU_ERF) {
+                    // lane = row: alpha, the column's bias (the same for every
+                    // lane) and Relu straight on the accumulators, then the
+                    // finished block goes out by TMA -- no read-back
+                    const bool relu = epi == LONNX_EPI_RELU;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float4 b4 = *reinterpret_cast<const float4 *>(sbg + ch * 16 + 4 * u);  // broadcast
+                        const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+                        float v[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            float x = acc[ch * 16 + 4 * u + k];
+                            if (alpha != 1.0f) x = __fmul_rn(x, alpha);
+                            if (bias) x = __fadd_rn(x, bb[k]);
+                            v[k] = (relu && !(x > 0.0f)) ? 0.0f : x;
+                        }
+                        *reinterpret_cast<float4 *>(stg + sidx(lane, u)) = make_float4(v[0], v[1], v[2], v[3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && cbase + ch * 16 < N) {
+                        tma_store_2d(&tmC, smem_u32(stg), cbase + ch * 16, rbase);
+                        bulk_commit_group();
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
                     *reinterpret_cast<float4 *>(stg + sidx(lane, u)) = make_float4(
