@@ -25,13 +25,31 @@ def shard_inputs(inputs: dict, world: int, rank: int) -> dict:
     return {k: np.ascontiguousarray(v[lo:hi]) for k, v in inputs.items()}
 
 
-def gather_outputs(local: dict, group=None) -> dict:
-    """Concatenate each rank's host outputs in rank order (host-side gather)."""
+def gather_outputs(local: dict, group=None, batch: int | None = None) -> dict:
+    """Concatenate each rank's host outputs in rank order (host-side gather).
+
+    With ``batch`` (the global row count) every output is moved as one
+    tensor all_gather of the ceil(batch / world) rows each rank may hold --
+    no pickling; without it, as Python objects."""
+    import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
-    parts = [None] * world
-    dist.all_gather_object(parts, local, group=group)
-    return {k: np.concatenate([p[k] for p in parts], axis=0) for k in local}
+    if batch is None:
+        parts = [None] * world
+        dist.all_gather_object(parts, local, group=group)
+        return {k: np.concatenate([p[k] for p in parts], axis=0) for k in local}
+    per = -(-batch // world)
+    out = {}
+    for k in sorted(local):
+        a = np.ascontiguousarray(local[k])
+        buf = np.zeros((per,) + a.shape[1:], a.dtype)
+        buf[:a.shape[0]] = a
+        t = torch.from_numpy(buf)
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t, group=group)
+        out[k] = np.concatenate([parts[r].numpy()[:shard_bounds(batch, world, r)[1] - shard_bounds(batch, world, r)[0]]
+                                 for r in range(world)], axis=0)
+    return out
 
 
 def run_sharded(execute, inputs: dict, group=None) -> dict:
@@ -39,4 +57,5 @@ def run_sharded(execute, inputs: dict, group=None) -> dict:
     full-batch outputs on every rank."""
     import torch.distributed as dist
     world, rank = dist.get_world_size(group), dist.get_rank(group)
-    return gather_outputs(execute(shard_inputs(inputs, world, rank)), group)
+    batch = next(iter(inputs.values())).shape[0]
+    return gather_outputs(execute(shard_inputs(inputs, world, rank)), group, batch)
