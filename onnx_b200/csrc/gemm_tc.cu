@@ -67,18 +67,25 @@ constexpr int MODE_GEMM = 0, MODE_CONV = 1, MODE_CONV_RES = 2;
 // previous phase is complete whenever j - S <= j - CH - 1, i.e. S >= CH + 1.
 // (CH = 4 with a 3-stage ring broke this and faulted.)
 constexpr int CH = 2;
+// Drain groups (chunk_group_pos): GRP chunks of one TMEM buffer are summed
+// by the tensor core before a drain, a truncating sum of GRP * CH * BK = 192
+// terms at most; the issuers' alternation, and so the invariant above, is
+// unchanged.  Groups are what lets the next tile's MMAs run under an
+// epilogue: with one drain per chunk they stopped two chunks into it.
+constexpr int GRP = 3;
 
 // Role timeline of CTA 0 (clock64), compiled only into a diagnostic build
 // (-DLONNX_GEMM_TIMELINE); read back with lonnx_debug_gemm_timeline.
 // [0, 256): issuer start of chunk c, [256, 512): issuer commit of chunk c,
 // [512, 768): accumulator warp 8 past tfull of chunk c, [768, 1024): its
 // tdrain arrive, [1024, 1040): epilogue start of tile t, [1040, 1056): end,
-// [1056, 1184): 8 marks inside the epilogue of tile t (t < 16).
+// [1056, 1184): 8 marks inside the epilogue of tile t (t < 16), [1184]:
+// kernel entry, [1185]: past the dependency wait.
 #ifdef LONNX_GEMM_TIMELINE
-__device__ long long g_gemm_tl[1184];
+__device__ long long g_gemm_tl[1192];
 #define GTL(off, idx)                                                                      \
     do {                                                                                   \
-        if (blockIdx.x == 0 && (idx) < ((off) >= 1056 ? 128 : (off) >= 1024 ? 16 : 256)) \
+        if (blockIdx.x == 0 && (idx) < ((off) >= 1184 ? 8 : (off) >= 1056 ? 128 : (off) >= 1024 ? 16 : 256)) \
             g_gemm_tl[(off) + (idx)] = clock64();                                          \
     } while (0)
 #else
@@ -200,6 +207,15 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     auto tile_n0 = [&](int t) { return (t % ntn) * BN; };
     auto tile_m0 = [&](int t) { return (t / ntn) * BM; };
     auto step_tile = [&](int j) { return (int)blockIdx.x + (j / nk) * (int)gridDim.x; };
+    // drain groups: the chunks of one tile that land in the same TMEM
+    // buffer (every other chunk) are summed there GRP at a time before the
+    // accumulator warps add them into registers, so the MMAs of a tile's
+    // first 2 * GRP chunks need no drain and run under the previous tile's
+    // epilogue.  gpos: the chunk's place in its group; a group ends after
+    // GRP chunks or with the buffer's last chunk of the tile.
+    // (the chunks of a tile in one buffer are those of one parity of ci)
+    auto chunk_group_pos = [&](int ci) { return (ci >> 1) % GRP; };
+    auto chunk_group_last = [&](int ci, int gpos) { return gpos == GRP - 1 || ci + 2 >= nch; };
 
     auto full = [&](int s) { return smem_u32(bars + s); };
     auto conv = [&](int s) { return smem_u32(bars + S + s); };
@@ -214,6 +230,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     int issued = 0;
 
     if (threadIdx.x == 0) {
+        GTL(1184, 0);
         for (int s = 0; s < S; ++s) {
             mbar_init(full(s), 1);
             mbar_init(conv(s), 4 * NAG);  // one arrive per A warp
@@ -256,6 +273,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     // set-up done: wait for the previous kernel's results (launched with PDL)
     pdl_wait();
     pdl_trigger();
+    if (threadIdx.x == 0) GTL(1185, 0);
     bool ok = true;
     const int agroup = (warp >= W_A0 && warp < W_A0 + 4) ? 0 : (NAG == 2 && warp >= G::W_A1 && warp < G::W_A1 + 4) ? 1 : -1;
 
@@ -296,10 +314,16 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             // chunk cidx = CH consecutive K stages of one tile, accumulated
             // by the tensor core into TMEM chunk buffer cidx & 1; issuer
             // (cidx & 1) owns that buffer, so a chunk's stages are ordered
+            int grp_n = 0;  // drain groups of buffer b begun so far
             for (int cidx = warp - W_MMA; cidx < total_ch && ok; cidx += 2) {
                 const int tt = cidx / nch, ci = cidx - tt * nch, b = cidx & 1;
                 const int i0 = ci * CH, i1 = min(nk, i0 + CH);
-                if (!mbar_wait(tdrain(b), ((cidx >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+                const int gpos = chunk_group_pos(ci);
+                if (gpos == 0) {
+                    // a fresh group: the buffer's previous group must be drained
+                    if (!mbar_wait(tdrain(b), (grp_n & 1) ^ 1, abort_flag)) { ok = false; break; }
+                    ++grp_n;
+                }
                 GTL(0, cidx);
                 const uint32_t acc = tmem + G::ACC_COL + b * BN;
                 for (int i = i0; i < i1 && ok; ++i) {
@@ -316,14 +340,14 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
 #pragma unroll
                     for (int kk = 0; kk < BK / 8; ++kk) {
                         const uint64_t dw = smem_desc_sw128(w + kk * 32), dwl = smem_desc_sw128(wlo + kk * 32);
-                        mma_tf32_ts(acc, alo + kk * 8, dw, idesc, (i != i0) || kk != 0);
+                        mma_tf32_ts(acc, alo + kk * 8, dw, idesc, gpos != 0 || i != i0 || kk != 0);
                         mma_tf32_ts(acc, ahi + kk * 8, dwl, idesc, 1);
                         mma_tf32_ts(acc, ahi + kk * 8, dw, idesc, 1);
                     }
                     mma_commit(empty(s));
                     mma_commit(afree(ab));
                 }
-                if (ok) mma_commit(tfull(b));
+                if (ok && chunk_group_last(ci, gpos)) mma_commit(tfull(b));
                 GTL(256, cidx);
             }
         }
@@ -548,6 +572,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         const int q = warp & 3, grp = (warp - W_ACC0) >> 2;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::ACC_COL + grp * 64;
         const int rloc = q * 32 + lane;
+        int drained0 = 0, drained1 = 0;  // drain groups of buffers 0 and 1 so far
         for (int tt = 0; tt < my_tiles && ok; ++tt) {
             const int t = t0 + tt * (int)gridDim.x, n0 = tile_n0(t), m0 = tile_m0(t);
             if constexpr (RES) {
@@ -572,7 +597,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
             for (int ci = 0; ci < nch && ok; ++ci) {
                 const int cidx = tt * nch + ci, b = cidx & 1;
-                if (!mbar_wait(tfull(b), (cidx >> 1) & 1, abort_flag)) { ok = false; break; }
+                if (!chunk_group_last(ci, chunk_group_pos(ci))) continue;  // the group goes on in TMEM
+                const int gn = b ? drained1++ : drained0++;
+                if (!mbar_wait(tfull(b), gn & 1, abort_flag)) { ok = false; break; }
                 if (warp == W_ACC0 && lane == 0) GTL(512, cidx);
                 tc_fence_after();
 #pragma unroll
@@ -1372,7 +1399,7 @@ int split_tf32_nk(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int K, i
 
 #ifdef LONNX_GEMM_TIMELINE
 extern "C" LONNX_API int lonnx_debug_gemm_timeline(long long *host, int n) {
-    LONNX_CUDA(cudaMemcpyFromSymbol(host, g_gemm_tl, sizeof(long long) * (n < 1184 ? n : 1184)));
+    LONNX_CUDA(cudaMemcpyFromSymbol(host, g_gemm_tl, sizeof(long long) * (n < 1192 ? n : 1192)));
     return LONNX_OK;
 }
 #endif
