@@ -780,6 +780,392 @@ k_attention_pf(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     }
 }
 
+// ---------------------------------------------------------------------------
+// k_attention_ws: warp-specialised, persistent, one CTA per SM.
+//
+// The per-pair chain of k_attention_pf (load, split, S = Q K^T, softmax,
+// O += E V, store) ran in lock step with six block barriers, so one pair took
+// ~20k cycles and only two were in flight per SM.  Here each step has its own
+// warps and the pairs i, i + 1 overlap:
+//   warp 0   TMA: Q, K of pair i into slot i % 2 once S(i - 2) is done; V of
+//            pair i into one staging tile once V(i - 1) has been transposed;
+//   warp 1   S(i) = Q K^T into TMEM S[i % 2] (12 MMAs, A and B from shared
+//            memory) once S[i % 2] is free, i.e. P.V(i - 2) is done;
+//   warp 2   O(i) = E V into TMEM O[i % 2]: per 8 keys one MMA with the
+//            merged B operand [V^T | V^T_lo] (N = 64: columns 0-31 get E V,
+//            32-63 E V_lo) and one of E_lo V (N = 32, into columns 0-31), the
+//            same products and order as k_attention_pf in 32 MMAs instead of 48;
+//   warps 4-7  per row: Q_lo, K_lo beside Q, K; the mask (log2 units); V
+//            transposed into V^T / V^T_lo of the slot;
+//   warps 8-15 softmax of pair i (two threads per row, keys split as in
+//            k_attention_pf): E over S[i % 2] in place, E_lo kept in registers
+//            until P.V(i - 1) has released the E_lo columns; then the
+//            epilogue of pair i - 1 (O / row sum -> out).
+// TMEM (512 columns): S0 [0, 128), S1 [128, 256), O0 [256, 320), O1
+// [320, 384), E_lo [384, 512).  Shared memory: two 96 KB slots (Q, Q_lo, K,
+// K_lo, [V^T | V^T_lo] as four 8 KB K-atoms of 64 rows), a 16 KB V staging
+// tile, masks and the row max / sum exchange.  Every mbarrier wait is
+// bounded and a failed one raises the CTA's abort flag at once; the named
+// barriers of the softmax and prep warps reduce an "abort" predicate
+// (bar.red.or), so those warps stop together; on expiry the CTA records
+// LONNX_E_TIMEOUT, drains its MMAs and loads, frees TMEM and returns.
+constexpr int WS_THREADS = 512;
+constexpr int WS_SLOT = 6 * TILE;                 // Q, Q_lo, K, K_lo, VV (2 tiles)
+constexpr int WS_Q = 0, WS_QLO = TILE, WS_K = 2 * TILE, WS_KLO = 3 * TILE, WS_VV = 4 * TILE;
+constexpr int WS_VST = 2 * WS_SLOT;               // V staging tile
+constexpr int WS_MSK = WS_VST + TILE;             // [2][128] floats
+constexpr int WS_RED = WS_MSK + 2 * 128 * 4;      // max [2][2][128], sum [2][2][128]
+constexpr int WS_BAR = WS_RED + 8 * 128 * 4;
+constexpr int WS_SMEM = WS_BAR + 256 + 1024;
+constexpr uint32_t WS_COL_S = 0, WS_COL_O = 256, WS_COL_ELO = 384;
+enum {
+    WB_FULLQK = 0, WB_FULLV = 2, WB_VFREE = 3, WB_PREPQK = 4, WB_PREPV = 6, WB_SFULL = 8, WB_EFULL = 10,
+    WB_OFULL = 12, WB_OFREE = 14, WB_DRAIN = 16, WB_COUNT = 17
+};
+
+// Phase marks of CTA 0 per pair (clock64), compiled only into a diagnostic
+// build (-DLONNX_ATTN_TIMELINE); read back with lonnx_debug_attention_ws_timeline.
+#ifdef LONNX_ATTN_TIMELINE
+__device__ long long g_attn_ws_tl[8 * 16];
+#define AWT(slot, i)                                                                  \
+    do {                                                                              \
+        if (blockIdx.x == 0 && (i) < 8) g_attn_ws_tl[(i) * 16 + (slot)] = clock64(); \
+    } while (0)
+#else
+#define AWT(slot, i) \
+    do {             \
+    } while (0)
+#endif
+
+// bar.sync on a named barrier that also ORs a predicate over its threads
+__device__ __forceinline__ bool bar_red_or(int id, int nthreads, bool pred) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\tselp.b32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((int)pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
+}
+
+// 2^x, flushing subnormal results to zero: one MUFU operation (the
+// non-flushing form cost ~10% of the kernel); terms below 2^-126 of a row's
+// largest term (which is 1) do not change its sum
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__global__ void __launch_bounds__(WS_THREADS, 1)
+k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+               const __grid_constant__ CUtensorMap tv, const float *__restrict__ maskadd, float *__restrict__ out,
+               int npairs, int S, int heads, float scale, int *dev_flags) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + WS_BAR);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + WB_COUNT);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *msk = reinterpret_cast<float *>(sm + WS_MSK);
+    float *red_max = reinterpret_cast<float *>(sm + WS_RED), *red_sum = red_max + 4 * 128;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    auto bar = [&](int i) { return smem_u32(bars + i); };
+    const int npc = (int)blockIdx.x < npairs ? (npairs - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    auto pair_of = [&](int i) { return (int)blockIdx.x + i * (int)gridDim.x; };
+
+    if (t == 0) {
+        for (int j = 0; j < 2; ++j) {
+            mbar_init(bar(WB_FULLQK + j), 1);
+            mbar_init(bar(WB_PREPQK + j), 4);  // one arrive per prep warp
+            mbar_init(bar(WB_PREPV + j), 1);
+            mbar_init(bar(WB_SFULL + j), 1);
+            mbar_init(bar(WB_EFULL + j), 8);   // one arrive per softmax warp
+            mbar_init(bar(WB_OFULL + j), 1);
+            mbar_init(bar(WB_OFREE + j), 8);
+        }
+        mbar_init(bar(WB_FULLV), 1);
+        mbar_init(bar(WB_VFREE), 1);
+        mbar_init(bar(WB_DRAIN), 2);  // the two MMA-issuing threads
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tq);
+        prefetch_tmap(&tk);
+        prefetch_tmap(&tv);
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // set-up done: wait for the QKV projection (launched with PDL)
+    pdl_wait();
+    pdl_trigger();
+    bool ok = true;
+    // a bounded wait; on expiry this thread stops and every role learns of it
+    auto wait = [&](int b, int parity) {
+        if (!ok) return false;
+        if (!mbar_wait(bar(b), (uint32_t)parity & 1u, abort_flag)) {
+            ok = false;
+            *abort_flag = 1;
+        }
+        return ok;
+    };
+    int pend_qk0 = 0, pend_qk1 = 0, pend_v = 0;  // warp 0: loads issued (for the abort drain)
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int i = 0; i < npc && ok; ++i) {
+                const int s = i & 1, pr = pair_of(i), b = pr / heads, h = pr - b * heads;
+                // slot s: Q, K, Q_lo, K_lo last read by S(i - 2)
+                if (i >= 2 && !wait(WB_SFULL + s, (i - 2) >> 1)) break;
+                mbar_arrive_expect_tx(bar(WB_FULLQK + s), 2 * TILE);
+                tma_load_2d(smem_u32(sm + s * WS_SLOT + WS_Q), &tq, bar(WB_FULLQK + s), h * DH, b * S);
+                tma_load_2d(smem_u32(sm + s * WS_SLOT + WS_K), &tk, bar(WB_FULLQK + s), h * DH, b * S);
+                if (s) ++pend_qk1; else ++pend_qk0;
+                // the staging tile: V(i - 1) transposed
+                if (i >= 1 && !wait(WB_VFREE, i - 1)) break;
+                mbar_arrive_expect_tx(bar(WB_FULLV), TILE);
+                tma_load_2d(smem_u32(sm + WS_VST), &tv, bar(WB_FULLV), h * DH, b * S);
+                ++pend_v;
+                AWT(0, i);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_tf32(128, 128);
+            for (int i = 0; i < npc && ok; ++i) {
+                const int s = i & 1;
+                if (!wait(WB_PREPQK + s, i >> 1)) break;
+                // S[s] held E(i - 2), the A operand of P.V(i - 2)
+                if (i >= 2 && !wait(WB_OFULL + s, (i - 2) >> 1)) break;
+                tc_fence_after();
+                AWT(1, i);
+                const uint8_t *sl = sm + s * WS_SLOT;
+                const uint32_t a = smem_u32(sl + WS_Q), al = smem_u32(sl + WS_QLO);
+                const uint32_t bk = smem_u32(sl + WS_K), bl = smem_u32(sl + WS_KLO);
+                const uint32_t d = tmem + WS_COL_S + s * 128;
+#pragma unroll
+                for (int kk = 0; kk < DH / 8; ++kk) {
+                    const uint32_t ko = kk * 32;
+                    mma_tf32(d, smem_desc_sw128(al + ko), smem_desc_sw128(bk + ko), idesc, kk != 0);
+                    mma_tf32(d, smem_desc_sw128(a + ko), smem_desc_sw128(bl + ko), idesc, 1);
+                    mma_tf32(d, smem_desc_sw128(a + ko), smem_desc_sw128(bk + ko), idesc, 1);
+                }
+                mma_commit(bar(WB_SFULL + s));
+            }
+        }
+    } else if (warp == 2) {
+        if (lane == 0) {
+            constexpr uint32_t id64 = idesc_tf32(128, 64), id32 = idesc_tf32(128, DH);
+            for (int i = 0; i < npc && ok; ++i) {
+                const int s = i & 1;
+                if (!wait(WB_EFULL + s, i >> 1)) break;
+                if (!wait(WB_PREPV + s, i >> 1)) break;
+                // O[s] was read by the epilogue of pair i - 2
+                if (i >= 2 && !wait(WB_OFREE + s, (i - 2) >> 1)) break;
+                tc_fence_after();
+                AWT(2, i);
+                const uint32_t o = tmem + WS_COL_O + s * 64;
+                const uint32_t vv = smem_u32(sm + s * WS_SLOT + WS_VV);
+#pragma unroll
+                for (int kk = 0; kk < 16; ++kk) {
+                    const uint64_t bd = smem_desc_sw128(vv + (kk >> 2) * (64 * ROWB) + (kk & 3) * 32);
+                    mma_tf32_ts(o, tmem + WS_COL_S + s * 128 + kk * 8, bd, id64, kk != 0);  // E [V | V_lo]
+                    mma_tf32_ts(o, tmem + WS_COL_ELO + kk * 8, bd, id32, 1);               // E_lo V
+                }
+                mma_commit(bar(WB_OFULL + s));
+                AWT(3, i);
+            }
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ---- prep: one row (query / key) per thread ----------------------------
+        const int r = t - 128;
+        const bool live = r < S;
+        const int atom = r >> 5, ch = (r & 31) >> 2, wd = r & 3;
+        for (int i = 0; i < npc; ++i) {
+            const int s = i & 1, pr = pair_of(i), b = pr / heads;
+            uint8_t *sl = sm + s * WS_SLOT;
+            const float mv = (maskadd && live) ? maskadd[(int64_t)b * S + r] : 0.0f;
+            if (wait(WB_FULLQK + s, i >> 1)) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const int o = swz(r, c);
+                    *reinterpret_cast<float4 *>(sl + WS_QLO + o) = lo4(*reinterpret_cast<const float4 *>(sl + WS_Q + o));
+                    *reinterpret_cast<float4 *>(sl + WS_KLO + o) = lo4(*reinterpret_cast<const float4 *>(sl + WS_K + o));
+                }
+            }
+            // msk[s] was read by the softmax of pair i - 2
+            if (i < 2 || wait(WB_EFULL + s, (i - 2) >> 1))
+                if (ok) msk[s * 128 + r] = mv * kLog2e;
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(bar(WB_PREPQK + s));
+            // V: staging tile -> [V^T | V^T_lo] of the slot, once P.V(i - 2) is done with it
+            wait(WB_FULLV, i);
+            if (i >= 2) wait(WB_OFULL + s, (i - 2) >> 1);
+            if (ok) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const float4 v4 = *reinterpret_cast<const float4 *>(sm + WS_VST + swz(r, c));
+                    const float e4[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int d = c * 4 + u;
+                        const float x = live ? e4[u] : 0.0f;
+                        const int off = atom * 64 * ROWB + wd * 4;
+                        *reinterpret_cast<float *>(sl + WS_VV + off + swz(d, ch)) = x;
+                        *reinterpret_cast<float *>(sl + WS_VV + off + swz(d + 32, ch)) = __fsub_rn(x, tf32_hi(x));
+                    }
+                }
+            }
+            fence_proxy_async_smem();
+            if (bar_red_or(2, 128, !ok || *abort_flag)) {
+                ok = false;
+                *abort_flag = 1;
+                break;
+            }
+            if (r == 0) {
+                mbar_arrive(bar(WB_VFREE));      // the staging tile has been read
+                mbar_arrive(bar(WB_PREPV + s));  // V^T / V^T_lo of slot s written
+            }
+        }
+    } else if (warp >= 8) {
+        // ---- softmax of pair i, then the epilogue of pair i - 1 -----------------
+        const int g = (warp - 8) >> 2, row = (warp & 3) * 32 + lane;
+        const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const float c2 = kLog2e / scale;
+        auto epilogue = [&](int i) {
+            const int s = i & 1, pr = pair_of(i), b = pr / heads, h = pr - b * heads;
+            tc_fence_after();
+            uint32_t oa[16], ob[16];
+            tmem_ld_32x32b_x16(lane_addr + WS_COL_O + s * 64 + g * 16, oa);
+            tmem_ld_32x32b_x16(lane_addr + WS_COL_O + s * 64 + 32 + g * 16, ob);
+            tmem_ld_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(WB_OFREE + s));
+            if (row < S) {
+                const float inv = 1.0f / (red_sum[s * 256 + row] + red_sum[s * 256 + 128 + row]);
+                float *op = out + ((int64_t)b * S + row) * ((int64_t)heads * DH) + (int64_t)h * DH + g * 16;
+#pragma unroll
+                for (int d = 0; d < 16; d += 4) {
+                    float v4[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        v4[u] = __fadd_rn(__uint_as_float(oa[d + u]), __uint_as_float(ob[d + u])) * inv;
+                    *reinterpret_cast<float4 *>(op + d) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+                }
+            }
+        };
+        bool stop = false;
+        for (int i = 0; i < npc; ++i) {
+            const int s = i & 1;
+            const float *mk = msk + s * 128;
+            wait(WB_SFULL + s, i >> 1);
+            wait(WB_PREPQK + s, i >> 1);  // the mask
+            tc_fence_after();
+            if (warp == 8 && lane == 0) AWT(4, i);
+            uint32_t r0[32], r1[32];
+            float mx = 0.0f;  // the reference's running max starts at 0; 0 maps to 0 in log2 units
+            if (ok) {
+                tmem_ld_32x32b_x32(lane_addr + WS_COL_S + s * 128 + g * 32, r0);
+                tmem_ld_32x32b_x32(lane_addr + WS_COL_S + s * 128 + 64 + g * 32, r1);
+                tmem_ld_wait();
+                // u = s log2(e) / scale + mask log2(e), kept in r0 / r1 for the
+                // exponent pass; keys past S get -inf (2^-inf = 0)
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    const float4 m0 = *reinterpret_cast<const float4 *>(mk + g * 32 + j4 * 4);
+                    const float4 m1 = *reinterpret_cast<const float4 *>(mk + 64 + g * 32 + j4 * 4);
+                    const float ma[4] = {m0.x, m0.y, m0.z, m0.w}, mb[4] = {m1.x, m1.y, m1.z, m1.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int j = j4 * 4 + u, k0 = g * 32 + j, k1 = 64 + g * 32 + j;
+                        const float u0 = k0 < S ? fmaf(__uint_as_float(r0[j]), c2, ma[u]) : -INFINITY;
+                        const float u1 = k1 < S ? fmaf(__uint_as_float(r1[j]), c2, mb[u]) : -INFINITY;
+                        mx = fmaxf(mx, u0);
+                        mx = fmaxf(mx, u1);
+                        r0[j] = __float_as_uint(u0);
+                        r1[j] = __float_as_uint(u1);
+                    }
+                }
+            }
+            red_max[s * 256 + g * 128 + row] = mx;
+            if (bar_red_or(1, 256, !ok || *abort_flag)) {
+                stop = true;
+                break;
+            }
+            mx = fmaxf(red_max[s * 256 + row], red_max[s * 256 + 128 + row]);
+            // E over S[s] in place now; E_lo into r0 / r1 until the E_lo columns are free
+            float sum = 0.0f;
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t(&r)[32] = hf ? r1 : r0;
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    uint32_t eh[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float e = ex2_ftz(__uint_as_float(r[q * 16 + j]) - mx);
+                        sum += e;
+                        eh[j] = __float_as_uint(e);
+                        r[q * 16 + j] = __float_as_uint(__fsub_rn(e, tf32_hi(e)));
+                    }
+                    tmem_st_32x32b_x16(lane_addr + WS_COL_S + s * 128 + hf * 64 + g * 32 + q * 16, eh);
+                }
+            }
+            red_sum[s * 256 + g * 128 + row] = sum;
+            // E_lo columns: last read by P.V(i - 1)
+            if (i >= 1) wait(WB_OFULL + (s ^ 1), (i - 1) >> 1);
+            tc_fence_after();
+            if (ok) {
+                tmem_st_32x32b_x32(lane_addr + WS_COL_ELO + g * 32, r0);
+                tmem_st_32x32b_x32(lane_addr + WS_COL_ELO + 64 + g * 32, r1);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(bar(WB_EFULL + s));
+            if (warp == 8 && lane == 0) AWT(5, i);
+            if (ok && i >= 1) epilogue(i - 1);
+        }
+        // the last pair: its row sums need the partner thread's
+        if (!stop && npc > 0) {
+            const int last = npc - 1;
+            wait(WB_OFULL + (last & 1), last >> 1);
+            if (!bar_red_or(1, 256, !ok || *abort_flag)) epilogue(last);
+        }
+    }
+
+    if (!ok) *abort_flag = 1;
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag) {
+        if (t == 0) atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
+        // drain: MMAs issued by the two issuing threads, TMA loads in flight
+        if (t == 32 || t == 64) {
+            mma_commit(bar(WB_DRAIN));
+            mbar_wait(bar(WB_DRAIN), 0, nullptr, 400000000ll);
+        }
+        if (t == 0) {
+            // the (pend - 1)-th completion of a load barrier is the last one issued
+            if (pend_qk0) mbar_wait(bar(WB_FULLQK), (pend_qk0 - 1) & 1, nullptr, 400000000ll);
+            if (pend_qk1) mbar_wait(bar(WB_FULLQK + 1), (pend_qk1 - 1) & 1, nullptr, 400000000ll);
+            if (pend_v) mbar_wait(bar(WB_FULLV), (pend_v - 1) & 1, nullptr, 400000000ll);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 }  // namespace
 
 namespace lonnx {
@@ -800,6 +1186,18 @@ int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v,
         if (!rc) rc = make_tile_map_f32(&mv, v, rows, cols, ld, 128);
         if (rc) return rc;
         static const bool tc8 = getenv("LONNX_ATTN_TC8") != nullptr;
+        static const bool pf = getenv("LONNX_ATTN_PF") != nullptr;
+        if (!tc8 && !pf) {
+            static bool attr_ws_set[64] = {false};
+            if (!attr_ws_set[ctx->device & 63]) {
+                LONNX_CUDA(cudaFuncSetAttribute(k_attention_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, WS_SMEM));
+                attr_ws_set[ctx->device & 63] = true;
+            }
+            const int npairs = B * heads;
+            const int grid = npairs < ctx->num_sms ? npairs : ctx->num_sms;  // one CTA per SM
+            return launch_pdl(ctx, k_attention_ws, dim3(grid), dim3(WS_THREADS), (size_t)WS_SMEM, mq, mk, mv, mask,
+                              out, npairs, S, heads, scale, ctx->dev_flags);
+        }
         if (!tc8) {
             static bool attr_pf_set[64] = {false};
             if (!attr_pf_set[ctx->device & 63]) {
@@ -834,6 +1232,10 @@ int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v,
 #ifdef LONNX_ATTN_TIMELINE
 extern "C" LONNX_API int lonnx_debug_attention_timeline(long long *host, int n) {
     LONNX_CUDA(cudaMemcpyFromSymbol(host, g_attn_tl, sizeof(long long) * (n < 256 ? n : 256)));
+    return LONNX_OK;
+}
+extern "C" LONNX_API int lonnx_debug_attention_ws_timeline(long long *host, int n) {
+    LONNX_CUDA(cudaMemcpyFromSymbol(host, g_attn_ws_tl, sizeof(long long) * (n < 128 ? n : 128)));
     return LONNX_OK;
 }
 #endif
