@@ -788,7 +788,7 @@ k_attention_pf(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 // ~20k cycles and only two were in flight per SM.  Here each step has its own
 // warps and the pairs i, i + 1 overlap:
 //   warp 0   TMA: Q, K of pair i into slot i % 2 once S(i - 2) is done; V of
-//            pair i into one staging tile once V(i - 1) has been transposed;
+//            pair i into the slot's V^T area once P.V(i - 2) is done;
 //   warp 1   S(i) = Q K^T into TMEM S[i % 2] (12 MMAs, A and B from shared
 //            memory) once S[i % 2] is free, i.e. P.V(i - 2) is done;
 //   warp 2   O(i) = E V into TMEM O[i % 2]: per 8 keys one MMA with the
@@ -796,30 +796,35 @@ k_attention_pf(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 //            32-63 E V_lo) and one of E_lo V (N = 32, into columns 0-31), the
 //            same products and order as k_attention_pf in 32 MMAs instead of 48;
 //   warps 4-7  per row: Q_lo, K_lo beside Q, K; the mask (log2 units); V
-//            transposed into V^T / V^T_lo of the slot;
-//   warps 8-15 softmax of pair i (two threads per row, keys split as in
-//            k_attention_pf): E over S[i % 2] in place, E_lo kept in registers
+//            read into registers, then written back transposed as V^T / V^T_lo;
+//   warps 8-23 softmax of pair i (four threads per row, 32 keys each; with
+//            two per row the softmax warps could not hide their latency and
+//            set the pace): E over S[i % 2] in place, E_lo kept in registers
 //            until P.V(i - 1) has released the E_lo columns; then the
-//            epilogue of pair i - 1 (O / row sum -> out).
+//            epilogue of pair i - 1: O / row sum into a swizzled staging tile
+//            that one TMA store writes out (S rows of 128 bytes; per-thread
+//            16-byte stores to 32 rows at once were ~2k cycles per pair).
 // TMEM (512 columns): S0 [0, 128), S1 [128, 256), O0 [256, 320), O1
 // [320, 384), E_lo [384, 512).  Shared memory: two 96 KB slots (Q, Q_lo, K,
-// K_lo, [V^T | V^T_lo] as four 8 KB K-atoms of 64 rows), a 16 KB V staging
-// tile, masks and the row max / sum exchange.  Every mbarrier wait is
+// K_lo, [V^T | V^T_lo] as four 8 KB K-atoms of 64 rows; raw V lands in the
+// upper 16 KB), a 16 KB output staging tile, masks and the row max / sum
+// exchange.  Every mbarrier wait is
 // bounded and a failed one raises the CTA's abort flag at once; the named
 // barriers of the softmax and prep warps reduce an "abort" predicate
 // (bar.red.or), so those warps stop together; on expiry the CTA records
 // LONNX_E_TIMEOUT, drains its MMAs and loads, frees TMEM and returns.
-constexpr int WS_THREADS = 512;
+constexpr int WS_SMW = 16;                        // softmax warps: 4 per TMEM lane quarter
+constexpr int WS_THREADS = (8 + WS_SMW) * 32;
 constexpr int WS_SLOT = 6 * TILE;                 // Q, Q_lo, K, K_lo, VV (2 tiles)
 constexpr int WS_Q = 0, WS_QLO = TILE, WS_K = 2 * TILE, WS_KLO = 3 * TILE, WS_VV = 4 * TILE;
-constexpr int WS_VST = 2 * WS_SLOT;               // V staging tile
-constexpr int WS_MSK = WS_VST + TILE;             // [2][128] floats
-constexpr int WS_RED = WS_MSK + 2 * 128 * 4;      // max [2][2][128], sum [2][2][128]
-constexpr int WS_BAR = WS_RED + 8 * 128 * 4;
+constexpr int WS_OST = 2 * WS_SLOT;               // output staging tile (TMA store source)
+constexpr int WS_MSK = WS_OST + TILE;             // [2][128] floats
+constexpr int WS_RED = WS_MSK + 2 * 128 * 4;      // max [2][4][128], sum [2][4][128]
+constexpr int WS_BAR = WS_RED + 16 * 128 * 4;
 constexpr int WS_SMEM = WS_BAR + 256 + 1024;
 constexpr uint32_t WS_COL_S = 0, WS_COL_O = 256, WS_COL_ELO = 384;
 enum {
-    WB_FULLQK = 0, WB_FULLV = 2, WB_VFREE = 3, WB_PREPQK = 4, WB_PREPV = 6, WB_SFULL = 8, WB_EFULL = 10,
+    WB_FULLQK = 0, WB_FULLV = 2, WB_PREPQK = 4, WB_PREPV = 6, WB_SFULL = 8, WB_EFULL = 10,
     WB_OFULL = 12, WB_OFREE = 14, WB_DRAIN = 16, WB_COUNT = 17
 };
 
@@ -860,15 +865,15 @@ __device__ __forceinline__ float ex2_ftz(float x) {
 
 __global__ void __launch_bounds__(WS_THREADS, 1)
 k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-               const __grid_constant__ CUtensorMap tv, const float *__restrict__ maskadd, float *__restrict__ out,
-               int npairs, int S, int heads, float scale, int *dev_flags) {
+               const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
+               const float *__restrict__ maskadd, int npairs, int S, int heads, float scale, int *dev_flags) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + WS_BAR);
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + WB_COUNT);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     float *msk = reinterpret_cast<float *>(sm + WS_MSK);
-    float *red_max = reinterpret_cast<float *>(sm + WS_RED), *red_sum = red_max + 4 * 128;
+    float *red_max = reinterpret_cast<float *>(sm + WS_RED), *red_sum = red_max + 8 * 128;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     auto bar = [&](int i) { return smem_u32(bars + i); };
     const int npc = (int)blockIdx.x < npairs ? (npairs - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
@@ -877,21 +882,21 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     if (t == 0) {
         for (int j = 0; j < 2; ++j) {
             mbar_init(bar(WB_FULLQK + j), 1);
+            mbar_init(bar(WB_FULLV + j), 1);
             mbar_init(bar(WB_PREPQK + j), 4);  // one arrive per prep warp
             mbar_init(bar(WB_PREPV + j), 1);
             mbar_init(bar(WB_SFULL + j), 1);
-            mbar_init(bar(WB_EFULL + j), 8);   // one arrive per softmax warp
+            mbar_init(bar(WB_EFULL + j), WS_SMW);  // one arrive per softmax warp
             mbar_init(bar(WB_OFULL + j), 1);
-            mbar_init(bar(WB_OFREE + j), 8);
+            mbar_init(bar(WB_OFREE + j), WS_SMW);
         }
-        mbar_init(bar(WB_FULLV), 1);
-        mbar_init(bar(WB_VFREE), 1);
         mbar_init(bar(WB_DRAIN), 2);  // the two MMA-issuing threads
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tq);
         prefetch_tmap(&tk);
         prefetch_tmap(&tv);
+        prefetch_tmap(&to);
     }
     if (warp == 0) {
         tmem_alloc(smem_u32(tmem_slot), 512);
@@ -914,7 +919,7 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         }
         return ok;
     };
-    int pend_qk0 = 0, pend_qk1 = 0, pend_v = 0;  // warp 0: loads issued (for the abort drain)
+    int pend_qk0 = 0, pend_qk1 = 0, pend_v0 = 0, pend_v1 = 0;  // warp 0: loads issued (for the abort drain)
 
     if (warp == 0) {
         if (lane == 0) {
@@ -926,11 +931,11 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 tma_load_2d(smem_u32(sm + s * WS_SLOT + WS_Q), &tq, bar(WB_FULLQK + s), h * DH, b * S);
                 tma_load_2d(smem_u32(sm + s * WS_SLOT + WS_K), &tk, bar(WB_FULLQK + s), h * DH, b * S);
                 if (s) ++pend_qk1; else ++pend_qk0;
-                // the staging tile: V(i - 1) transposed
-                if (i >= 1 && !wait(WB_VFREE, i - 1)) break;
-                mbar_arrive_expect_tx(bar(WB_FULLV), TILE);
-                tma_load_2d(smem_u32(sm + WS_VST), &tv, bar(WB_FULLV), h * DH, b * S);
-                ++pend_v;
+                // raw V into the upper half of the slot's V^T area, read by P.V(i - 2)
+                if (i >= 2 && !wait(WB_OFULL + s, (i - 2) >> 1)) break;
+                mbar_arrive_expect_tx(bar(WB_FULLV + s), TILE);
+                tma_load_2d(smem_u32(sm + s * WS_SLOT + WS_VV + TILE), &tv, bar(WB_FULLV + s), h * DH, b * S);
+                if (s) ++pend_v1; else ++pend_v0;
                 AWT(0, i);
             }
         }
@@ -1004,14 +1009,22 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             fence_proxy_async_smem();
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(bar(WB_PREPQK + s));
-            // V: staging tile -> [V^T | V^T_lo] of the slot, once P.V(i - 2) is done with it
-            wait(WB_FULLV, i);
-            if (i >= 2) wait(WB_OFULL + s, (i - 2) >> 1);
+            // V (raw, in the upper half of the slot's V^T area; loaded after
+            // P.V(i - 2) was done with it) -> registers -> [V^T | V^T_lo]
+            float4 vr[8];
+            if (wait(WB_FULLV + s, i >> 1)) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) vr[c] = *reinterpret_cast<const float4 *>(sl + WS_VV + TILE + swz(r, c));
+            }
+            if (bar_red_or(2, 128, !ok || *abort_flag)) {  // every raw row read
+                ok = false;
+                *abort_flag = 1;
+                break;
+            }
             if (ok) {
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
-                    const float4 v4 = *reinterpret_cast<const float4 *>(sm + WS_VST + swz(r, c));
-                    const float e4[4] = {v4.x, v4.y, v4.z, v4.w};
+                    const float e4[4] = {vr[c].x, vr[c].y, vr[c].z, vr[c].w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int d = c * 4 + u;
@@ -1028,117 +1041,124 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 *abort_flag = 1;
                 break;
             }
-            if (r == 0) {
-                mbar_arrive(bar(WB_VFREE));      // the staging tile has been read
-                mbar_arrive(bar(WB_PREPV + s));  // V^T / V^T_lo of slot s written
-            }
+            if (r == 0) mbar_arrive(bar(WB_PREPV + s));  // V^T / V^T_lo of slot s written
         }
     } else if (warp >= 8) {
         // ---- softmax of pair i, then the epilogue of pair i - 1 -----------------
+        // thread (g, row): keys [32 g, 32 g + 32) of query row `row`
+        constexpr int NSM = WS_SMW * 32;
         const int g = (warp - 8) >> 2, row = (warp & 3) * 32 + lane;
         const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const float c2 = kLog2e / scale;
+        float *ost = reinterpret_cast<float *>(sm + WS_OST);
+        auto rowsum = [&](int s) {
+            const float *rs = red_sum + s * 512 + row;
+            return __fadd_rn(__fadd_rn(rs[0], rs[128]), __fadd_rn(rs[256], rs[384]));
+        };
+        // called by all softmax threads alike (it holds a named barrier);
+        // thread g writes output columns [8 g, 8 g + 8) of its row
         auto epilogue = [&](int i) {
             const int s = i & 1, pr = pair_of(i), b = pr / heads, h = pr - b * heads;
-            tc_fence_after();
-            uint32_t oa[16], ob[16];
-            tmem_ld_32x32b_x16(lane_addr + WS_COL_O + s * 64 + g * 16, oa);
-            tmem_ld_32x32b_x16(lane_addr + WS_COL_O + s * 64 + 32 + g * 16, ob);
-            tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(WB_OFREE + s));
-            if (row < S) {
-                const float inv = 1.0f / (red_sum[s * 256 + row] + red_sum[s * 256 + 128 + row]);
-                float *op = out + ((int64_t)b * S + row) * ((int64_t)heads * DH) + (int64_t)h * DH + g * 16;
+            if (ok) {
+                tc_fence_after();
+                uint32_t oa[8], ob[8];
+                tmem_ld_32x32b_x8(lane_addr + WS_COL_O + s * 64 + g * 8, oa);
+                tmem_ld_32x32b_x8(lane_addr + WS_COL_O + s * 64 + 32 + g * 8, ob);
+                tmem_ld_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(WB_OFREE + s));
+                const float inv = 1.0f / rowsum(s);
 #pragma unroll
-                for (int d = 0; d < 16; d += 4) {
+                for (int c = 0; c < 2; ++c) {
                     float v4[4];
 #pragma unroll
                     for (int u = 0; u < 4; ++u)
-                        v4[u] = __fadd_rn(__uint_as_float(oa[d + u]), __uint_as_float(ob[d + u])) * inv;
-                    *reinterpret_cast<float4 *>(op + d) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+                        v4[u] = __fadd_rn(__uint_as_float(oa[c * 4 + u]), __uint_as_float(ob[c * 4 + u])) * inv;
+                    *reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(ost) + swz(row, g * 2 + c)) =
+                        make_float4(v4[0], v4[1], v4[2], v4[3]);
                 }
+            }
+            fence_proxy_async_smem();
+            // rows >= S are not stored: the store's box is S rows high
+            if (!bar_red_or(3, NSM, !ok || *abort_flag) && t == 256) {
+                tma_store_2d(&to, smem_u32(ost), h * DH, b * S);
+                bulk_commit_group();
             }
         };
         bool stop = false;
         for (int i = 0; i < npc; ++i) {
             const int s = i & 1;
-            const float *mk = msk + s * 128;
+            const float *mk = msk + s * 128 + g * 32;
             wait(WB_SFULL + s, i >> 1);
             wait(WB_PREPQK + s, i >> 1);  // the mask
             tc_fence_after();
             if (warp == 8 && lane == 0) AWT(4, i);
-            uint32_t r0[32], r1[32];
+            uint32_t r[32];
             float mx = 0.0f;  // the reference's running max starts at 0; 0 maps to 0 in log2 units
             if (ok) {
-                tmem_ld_32x32b_x32(lane_addr + WS_COL_S + s * 128 + g * 32, r0);
-                tmem_ld_32x32b_x32(lane_addr + WS_COL_S + s * 128 + 64 + g * 32, r1);
+                tmem_ld_32x32b_x32(lane_addr + WS_COL_S + s * 128 + g * 32, r);
                 tmem_ld_wait();
-                // u = s log2(e) / scale + mask log2(e), kept in r0 / r1 for the
+                // u = s log2(e) / scale + mask log2(e), kept in r for the
                 // exponent pass; keys past S get -inf (2^-inf = 0)
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
-                    const float4 m0 = *reinterpret_cast<const float4 *>(mk + g * 32 + j4 * 4);
-                    const float4 m1 = *reinterpret_cast<const float4 *>(mk + 64 + g * 32 + j4 * 4);
-                    const float ma[4] = {m0.x, m0.y, m0.z, m0.w}, mb[4] = {m1.x, m1.y, m1.z, m1.w};
+                    const float4 m4 = *reinterpret_cast<const float4 *>(mk + j4 * 4);
+                    const float ma[4] = {m4.x, m4.y, m4.z, m4.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int j = j4 * 4 + u, k0 = g * 32 + j, k1 = 64 + g * 32 + j;
-                        const float u0 = k0 < S ? fmaf(__uint_as_float(r0[j]), c2, ma[u]) : -INFINITY;
-                        const float u1 = k1 < S ? fmaf(__uint_as_float(r1[j]), c2, mb[u]) : -INFINITY;
-                        mx = fmaxf(mx, u0);
-                        mx = fmaxf(mx, u1);
-                        r0[j] = __float_as_uint(u0);
-                        r1[j] = __float_as_uint(u1);
+                        const int j = j4 * 4 + u;
+                        const float x = g * 32 + j < S ? fmaf(__uint_as_float(r[j]), c2, ma[u]) : -INFINITY;
+                        mx = fmaxf(mx, x);
+                        r[j] = __float_as_uint(x);
                     }
                 }
             }
-            red_max[s * 256 + g * 128 + row] = mx;
-            if (bar_red_or(1, 256, !ok || *abort_flag)) {
+            red_max[s * 512 + g * 128 + row] = mx;
+            if (t == 256) bulk_wait_group_read0();  // the staging tile is free again after this barrier
+            if (bar_red_or(1, NSM, !ok || *abort_flag)) {
                 stop = true;
                 break;
             }
-            mx = fmaxf(red_max[s * 256 + row], red_max[s * 256 + 128 + row]);
-            // E over S[s] in place now; E_lo into r0 / r1 until the E_lo columns are free
+            {
+                const float *rm = red_max + s * 512 + row;
+                mx = fmaxf(fmaxf(rm[0], rm[128]), fmaxf(rm[256], rm[384]));
+            }
+            // E over S[s] in place now; E_lo into r until the E_lo columns are free
             float sum = 0.0f;
 #pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                uint32_t(&r)[32] = hf ? r1 : r0;
+            for (int q = 0; q < 2; ++q) {
+                uint32_t eh[16];
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    uint32_t eh[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float e = ex2_ftz(__uint_as_float(r[q * 16 + j]) - mx);
-                        sum += e;
-                        eh[j] = __float_as_uint(e);
-                        r[q * 16 + j] = __float_as_uint(__fsub_rn(e, tf32_hi(e)));
-                    }
-                    tmem_st_32x32b_x16(lane_addr + WS_COL_S + s * 128 + hf * 64 + g * 32 + q * 16, eh);
+                for (int j = 0; j < 16; ++j) {
+                    const float e = ex2_ftz(__uint_as_float(r[q * 16 + j]) - mx);
+                    sum += e;
+                    eh[j] = __float_as_uint(e);
+                    r[q * 16 + j] = __float_as_uint(__fsub_rn(e, tf32_hi(e)));
                 }
+                tmem_st_32x32b_x16(lane_addr + WS_COL_S + s * 128 + g * 32 + q * 16, eh);
             }
-            red_sum[s * 256 + g * 128 + row] = sum;
+            red_sum[s * 512 + g * 128 + row] = sum;
             // E_lo columns: last read by P.V(i - 1)
             if (i >= 1) wait(WB_OFULL + (s ^ 1), (i - 1) >> 1);
             tc_fence_after();
-            if (ok) {
-                tmem_st_32x32b_x32(lane_addr + WS_COL_ELO + g * 32, r0);
-                tmem_st_32x32b_x32(lane_addr + WS_COL_ELO + 64 + g * 32, r1);
-            }
+            if (ok) tmem_st_32x32b_x32(lane_addr + WS_COL_ELO + g * 32, r);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(bar(WB_EFULL + s));
             if (warp == 8 && lane == 0) AWT(5, i);
-            if (ok && i >= 1) epilogue(i - 1);
+            if (i >= 1) epilogue(i - 1);
+            if (warp == 8 && lane == 0) AWT(6, i);
         }
-        // the last pair: its row sums need the partner thread's
+        // the last pair: its row sums need the other threads' of the row
         if (!stop && npc > 0) {
             const int last = npc - 1;
             wait(WB_OFULL + (last & 1), last >> 1);
-            if (!bar_red_or(1, 256, !ok || *abort_flag)) epilogue(last);
+            if (t == 256) bulk_wait_group_read0();
+            if (!bar_red_or(1, NSM, !ok || *abort_flag)) epilogue(last);
         }
+        if (t == 256) bulk_wait_group0();  // every output tile written before the CTA exits
     }
 
     if (!ok) *abort_flag = 1;
@@ -1155,7 +1175,8 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             // the (pend - 1)-th completion of a load barrier is the last one issued
             if (pend_qk0) mbar_wait(bar(WB_FULLQK), (pend_qk0 - 1) & 1, nullptr, 400000000ll);
             if (pend_qk1) mbar_wait(bar(WB_FULLQK + 1), (pend_qk1 - 1) & 1, nullptr, 400000000ll);
-            if (pend_v) mbar_wait(bar(WB_FULLV), (pend_v - 1) & 1, nullptr, 400000000ll);
+            if (pend_v0) mbar_wait(bar(WB_FULLV), (pend_v0 - 1) & 1, nullptr, 400000000ll);
+            if (pend_v1) mbar_wait(bar(WB_FULLV + 1), (pend_v1 - 1) & 1, nullptr, 400000000ll);
         }
     }
     tc_fence_before();
@@ -1187,16 +1208,20 @@ int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v,
         if (rc) return rc;
         static const bool tc8 = getenv("LONNX_ATTN_TC8") != nullptr;
         static const bool pf = getenv("LONNX_ATTN_PF") != nullptr;
-        if (!tc8 && !pf) {
+        if (!tc8 && !pf && al16(out)) {
             static bool attr_ws_set[64] = {false};
             if (!attr_ws_set[ctx->device & 63]) {
                 LONNX_CUDA(cudaFuncSetAttribute(k_attention_ws, cudaFuncAttributeMaxDynamicSharedMemorySize, WS_SMEM));
                 attr_ws_set[ctx->device & 63] = true;
             }
+            // the output map: one store box per (sequence, head) = S rows x 32 columns
+            CUtensorMap mo;
+            rc = make_tile_map_f32(&mo, out, rows, cols, cols, S);
+            if (rc) return rc;
             const int npairs = B * heads;
             const int grid = npairs < ctx->num_sms ? npairs : ctx->num_sms;  // one CTA per SM
-            return launch_pdl(ctx, k_attention_ws, dim3(grid), dim3(WS_THREADS), (size_t)WS_SMEM, mq, mk, mv, mask,
-                              out, npairs, S, heads, scale, ctx->dev_flags);
+            return launch_pdl(ctx, k_attention_ws, dim3(grid), dim3(WS_THREADS), (size_t)WS_SMEM, mq, mk, mv, mo,
+                              mask, npairs, S, heads, scale, ctx->dev_flags);
         }
         if (!tc8) {
             static bool attr_pf_set[64] = {false};
