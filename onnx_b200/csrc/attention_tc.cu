@@ -791,21 +791,25 @@ k_attention_pf(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 //            pair i into the slot's V^T area once P.V(i - 2) is done;
 //   warp 1   S(i) = Q K^T into TMEM S[i % 2] (12 MMAs, A and B from shared
 //            memory) once S[i % 2] is free, i.e. P.V(i - 2) is done;
-//   warp 2   O(i) = E V into TMEM O[i % 2]: per 8 keys one MMA with the
-//            merged B operand [V^T | V^T_lo] (N = 64: columns 0-31 get E V,
-//            32-63 E V_lo) and one of E_lo V (N = 32, into columns 0-31), the
-//            same products and order as k_attention_pf in 32 MMAs instead of 48;
+//   warps 2, 3  O(i) = E V, issued by two threads (issuing one tcgen05.mma
+//            costs its thread ~110 cycles, and P.V set the pace from one):
+//            warp 2 per 8 keys one MMA with the merged B operand
+//            [V^T | V^T_lo] (N = 64: O columns 0-31 get E V, 32-63 E V_lo),
+//            warp 3 one of E_lo V (N = 32) into its own accumulator O_c;
 //   warps 4-7  per row: Q_lo, K_lo beside Q, K; the mask (log2 units); V
 //            read into registers, then written back transposed as V^T / V^T_lo;
 //   warps 8-23 softmax of pair i (four threads per row, 32 keys each; with
 //            two per row the softmax warps could not hide their latency and
 //            set the pace): E over S[i % 2] in place, E_lo kept in registers
-//            until P.V(i - 1) has released the E_lo columns; then the
-//            epilogue of pair i - 1: O / row sum into a swizzled staging tile
+//            until P.V(i - 1) has released the E_lo columns;
+//   warps 24-27 the epilogue of pair i as soon as P.V(i) is done (one row per
+//            thread): (O_a + O_c + O_b) / row sum into a swizzled staging tile
 //            that one TMA store writes out (S rows of 128 bytes; per-thread
 //            16-byte stores to 32 rows at once were ~2k cycles per pair).
-// TMEM (512 columns): S0 [0, 128), S1 [128, 256), O0 [256, 320), O1
-// [320, 384), E_lo [384, 512).  Shared memory: two 96 KB slots (Q, Q_lo, K,
+// TMEM (512 columns): S0 [0, 128), S1 [128, 256), O [256, 320) (E V | E V_lo),
+// O_c [320, 352) (E_lo V), E_lo [384, 512).  O is single-buffered: P.V(i)
+// waits for the epilogue of pair i - 1, which runs while pair i is in its
+// softmax.  Shared memory: two 96 KB slots (Q, Q_lo, K,
 // K_lo, [V^T | V^T_lo] as four 8 KB K-atoms of 64 rows; raw V lands in the
 // upper 16 KB), a 16 KB output staging tile, masks and the row max / sum
 // exchange.  Every mbarrier wait is
@@ -814,15 +818,19 @@ k_attention_pf(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 // (bar.red.or), so those warps stop together; on expiry the CTA records
 // LONNX_E_TIMEOUT, drains its MMAs and loads, frees TMEM and returns.
 constexpr int WS_SMW = 16;                        // softmax warps: 4 per TMEM lane quarter
-constexpr int WS_THREADS = (8 + WS_SMW) * 32;
+constexpr int WS_W_EPI = 8 + WS_SMW;              // first of the 4 epilogue warps
+constexpr int WS_THREADS = (WS_W_EPI + 4) * 32;
 constexpr int WS_SLOT = 6 * TILE;                 // Q, Q_lo, K, K_lo, VV (2 tiles)
 constexpr int WS_Q = 0, WS_QLO = TILE, WS_K = 2 * TILE, WS_KLO = 3 * TILE, WS_VV = 4 * TILE;
 constexpr int WS_OST = 2 * WS_SLOT;               // output staging tile (TMA store source)
 constexpr int WS_MSK = WS_OST + TILE;             // [2][128] floats
-constexpr int WS_RED = WS_MSK + 2 * 128 * 4;      // max [2][4][128], sum [2][4][128]
-constexpr int WS_BAR = WS_RED + 16 * 128 * 4;
+// row max [2][4][128]; row sums [4][4][128], by pair i % 4: the epilogue of
+// pair i reads them while the softmax of pair i + 2 runs (that of pair i + 3
+// comes after P.V(i + 1), which waits for the epilogue of pair i)
+constexpr int WS_RED = WS_MSK + 2 * 128 * 4;
+constexpr int WS_BAR = WS_RED + 24 * 128 * 4;
 constexpr int WS_SMEM = WS_BAR + 256 + 1024;
-constexpr uint32_t WS_COL_S = 0, WS_COL_O = 256, WS_COL_ELO = 384;
+constexpr uint32_t WS_COL_S = 0, WS_COL_O = 256, WS_COL_OC = 320, WS_COL_ELO = 384;
 enum {
     WB_FULLQK = 0, WB_FULLV = 2, WB_PREPQK = 4, WB_PREPV = 6, WB_SFULL = 8, WB_EFULL = 10,
     WB_OFULL = 12, WB_OFREE = 14, WB_DRAIN = 16, WB_COUNT = 17
@@ -887,10 +895,10 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             mbar_init(bar(WB_PREPV + j), 1);
             mbar_init(bar(WB_SFULL + j), 1);
             mbar_init(bar(WB_EFULL + j), WS_SMW);  // one arrive per softmax warp
-            mbar_init(bar(WB_OFULL + j), 1);
-            mbar_init(bar(WB_OFREE + j), WS_SMW);
+            mbar_init(bar(WB_OFULL + j), 2);  // one commit per P.V issuer
+            mbar_init(bar(WB_OFREE + j), 4);  // one arrive per epilogue warp (only [0] is used)
         }
-        mbar_init(bar(WB_DRAIN), 2);  // the two MMA-issuing threads
+        mbar_init(bar(WB_DRAIN), 3);  // the three MMA-issuing threads
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tq);
@@ -961,29 +969,41 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                     mma_tf32(d, smem_desc_sw128(a + ko), smem_desc_sw128(bk + ko), idesc, 1);
                 }
                 mma_commit(bar(WB_SFULL + s));
+#ifdef LONNX_ATTN_PROBE
+                mbar_wait(bar(WB_SFULL + s), (i >> 1) & 1, abort_flag);
+                AWT(7, i);
+#endif
             }
         }
-    } else if (warp == 2) {
+    } else if (warp == 2 || warp == 3) {
         if (lane == 0) {
-            constexpr uint32_t id64 = idesc_tf32(128, 64), id32 = idesc_tf32(128, DH);
+            const bool lo = warp == 3;
+            const uint32_t idesc = lo ? idesc_tf32(128, DH) : idesc_tf32(128, 64);
+            const uint32_t o = tmem + (lo ? WS_COL_OC : WS_COL_O);
             for (int i = 0; i < npc && ok; ++i) {
                 const int s = i & 1;
                 if (!wait(WB_EFULL + s, i >> 1)) break;
                 if (!wait(WB_PREPV + s, i >> 1)) break;
-                // O[s] was read by the epilogue of pair i - 2
-                if (i >= 2 && !wait(WB_OFREE + s, (i - 2) >> 1)) break;
+                // O, O_c were read by the epilogue of pair i - 1
+                if (i >= 1 && !wait(WB_OFREE, i - 1)) break;
                 tc_fence_after();
-                AWT(2, i);
-                const uint32_t o = tmem + WS_COL_O + s * 64;
+                if (!lo) AWT(2, i);
                 const uint32_t vv = smem_u32(sm + s * WS_SLOT + WS_VV);
+                const uint32_t a = tmem + (lo ? WS_COL_ELO : WS_COL_S + s * 128);
 #pragma unroll
                 for (int kk = 0; kk < 16; ++kk) {
+                    // E [V | V_lo] (N = 64) or E_lo V (N = 32: the first 32 rows of the same atom)
                     const uint64_t bd = smem_desc_sw128(vv + (kk >> 2) * (64 * ROWB) + (kk & 3) * 32);
-                    mma_tf32_ts(o, tmem + WS_COL_S + s * 128 + kk * 8, bd, id64, kk != 0);  // E [V | V_lo]
-                    mma_tf32_ts(o, tmem + WS_COL_ELO + kk * 8, bd, id32, 1);               // E_lo V
+                    mma_tf32_ts(o, a + kk * 8, bd, idesc, kk != 0);
                 }
                 mma_commit(bar(WB_OFULL + s));
-                AWT(3, i);
+                if (!lo) AWT(3, i);
+#ifdef LONNX_ATTN_PROBE
+                if (!lo) {
+                    mbar_wait(bar(WB_OFULL + s), (i >> 1) & 1, abort_flag);
+                    AWT(8, i);
+                }
+#endif
             }
         }
     } else if (warp >= 4 && warp < 8) {
@@ -991,10 +1011,16 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         const int r = t - 128;
         const bool live = r < S;
         const int atom = r >> 5, ch = (r & 31) >> 2, wd = r & 3;
+        // this row's mask entry, loaded one pair ahead
+        auto mask_of = [&](int i) {
+            return (maskadd && live && i < npc) ? __ldg(maskadd + (int64_t)(pair_of(i) / heads) * S + r) : 0.0f;
+        };
+        float mv_next = mask_of(0);
         for (int i = 0; i < npc; ++i) {
-            const int s = i & 1, pr = pair_of(i), b = pr / heads;
+            const int s = i & 1;
             uint8_t *sl = sm + s * WS_SLOT;
-            const float mv = (maskadd && live) ? maskadd[(int64_t)b * S + r] : 0.0f;
+            const float mv = mv_next;
+            mv_next = mask_of(i + 1);
             if (wait(WB_FULLQK + s, i >> 1)) {
 #pragma unroll
                 for (int c = 0; c < 8; ++c) {
@@ -1009,6 +1035,7 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             fence_proxy_async_smem();
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(bar(WB_PREPQK + s));
+            if (r == 0) AWT(9, i);
             // V (raw, in the upper half of the slot's V^T area; loaded after
             // P.V(i - 2) was done with it) -> registers -> [V^T | V^T_lo]
             float4 vr[8];
@@ -1042,51 +1069,15 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 break;
             }
             if (r == 0) mbar_arrive(bar(WB_PREPV + s));  // V^T / V^T_lo of slot s written
+            if (r == 0) AWT(10, i);
         }
-    } else if (warp >= 8) {
-        // ---- softmax of pair i, then the epilogue of pair i - 1 -----------------
+    } else if (warp >= 8 && warp < WS_W_EPI) {
+        // ---- softmax of pair i ----------------------------------------------------
         // thread (g, row): keys [32 g, 32 g + 32) of query row `row`
         constexpr int NSM = WS_SMW * 32;
         const int g = (warp - 8) >> 2, row = (warp & 3) * 32 + lane;
         const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const float c2 = kLog2e / scale;
-        float *ost = reinterpret_cast<float *>(sm + WS_OST);
-        auto rowsum = [&](int s) {
-            const float *rs = red_sum + s * 512 + row;
-            return __fadd_rn(__fadd_rn(rs[0], rs[128]), __fadd_rn(rs[256], rs[384]));
-        };
-        // called by all softmax threads alike (it holds a named barrier);
-        // thread g writes output columns [8 g, 8 g + 8) of its row
-        auto epilogue = [&](int i) {
-            const int s = i & 1, pr = pair_of(i), b = pr / heads, h = pr - b * heads;
-            if (ok) {
-                tc_fence_after();
-                uint32_t oa[8], ob[8];
-                tmem_ld_32x32b_x8(lane_addr + WS_COL_O + s * 64 + g * 8, oa);
-                tmem_ld_32x32b_x8(lane_addr + WS_COL_O + s * 64 + 32 + g * 8, ob);
-                tmem_ld_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(WB_OFREE + s));
-                const float inv = 1.0f / rowsum(s);
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    float v4[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        v4[u] = __fadd_rn(__uint_as_float(oa[c * 4 + u]), __uint_as_float(ob[c * 4 + u])) * inv;
-                    *reinterpret_cast<float4 *>(reinterpret_cast<uint8_t *>(ost) + swz(row, g * 2 + c)) =
-                        make_float4(v4[0], v4[1], v4[2], v4[3]);
-                }
-            }
-            fence_proxy_async_smem();
-            // rows >= S are not stored: the store's box is S rows high
-            if (!bar_red_or(3, NSM, !ok || *abort_flag) && t == 256) {
-                tma_store_2d(&to, smem_u32(ost), h * DH, b * S);
-                bulk_commit_group();
-            }
-        };
-        bool stop = false;
         for (int i = 0; i < npc; ++i) {
             const int s = i & 1;
             const float *mk = msk + s * 128 + g * 32;
@@ -1115,11 +1106,7 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 }
             }
             red_max[s * 512 + g * 128 + row] = mx;
-            if (t == 256) bulk_wait_group_read0();  // the staging tile is free again after this barrier
-            if (bar_red_or(1, NSM, !ok || *abort_flag)) {
-                stop = true;
-                break;
-            }
+            if (bar_red_or(1, NSM, !ok || *abort_flag)) break;
             {
                 const float *rm = red_max + s * 512 + row;
                 mx = fmaxf(fmaxf(rm[0], rm[128]), fmaxf(rm[256], rm[384]));
@@ -1138,7 +1125,7 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 }
                 tmem_st_32x32b_x16(lane_addr + WS_COL_S + s * 128 + g * 32 + q * 16, eh);
             }
-            red_sum[s * 512 + g * 128 + row] = sum;
+            red_sum[(i & 3) * 512 + g * 128 + row] = sum;
             // E_lo columns: last read by P.V(i - 1)
             if (i >= 1) wait(WB_OFULL + (s ^ 1), (i - 1) >> 1);
             tc_fence_after();
@@ -1148,17 +1135,61 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(bar(WB_EFULL + s));
             if (warp == 8 && lane == 0) AWT(5, i);
-            if (i >= 1) epilogue(i - 1);
-            if (warp == 8 && lane == 0) AWT(6, i);
         }
-        // the last pair: its row sums need the other threads' of the row
-        if (!stop && npc > 0) {
-            const int last = npc - 1;
-            wait(WB_OFULL + (last & 1), last >> 1);
-            if (t == 256) bulk_wait_group_read0();
-            if (!bar_red_or(1, NSM, !ok || *abort_flag)) epilogue(last);
+    } else if (warp >= WS_W_EPI) {
+        // ---- epilogue of pair i: one query row per thread -------------------------
+        const int r = t - WS_W_EPI * 32;
+        const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        uint8_t *ost = sm + WS_OST;
+        for (int i = 0; i < npc; ++i) {
+            const int s = i & 1, pr = pair_of(i), b = pr / heads, h = pr - b * heads;
+            wait(WB_EFULL + s, i >> 1);  // the row sums
+            wait(WB_OFULL + s, i >> 1);
+            tc_fence_after();
+            if (r == 0) bulk_wait_group_read0();  // the previous store has read the staging tile
+            if (bar_red_or(3, 128, !ok || *abort_flag)) {
+                ok = false;
+                *abort_flag = 1;
+                break;
+            }
+            const float *rs = red_sum + (i & 3) * 512 + r;
+            const float inv = 1.0f / __fadd_rn(__fadd_rn(rs[0], rs[128]), __fadd_rn(rs[256], rs[384]));
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t oa[16], ob[16], oc[16];
+                tmem_ld_32x32b_x16(lane_addr + WS_COL_O + hf * 16, oa);
+                tmem_ld_32x32b_x16(lane_addr + WS_COL_O + 32 + hf * 16, ob);
+                tmem_ld_32x32b_x16(lane_addr + WS_COL_OC + hf * 16, oc);
+                tmem_ld_wait();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float v4[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int k = c * 4 + u;
+                        const float ac = __fadd_rn(__uint_as_float(oa[k]), __uint_as_float(oc[k]));
+                        v4[u] = __fadd_rn(ac, __uint_as_float(ob[k])) * inv;
+                    }
+                    *reinterpret_cast<float4 *>(ost + swz(r, hf * 4 + c)) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(WB_OFREE));
+            fence_proxy_async_smem();
+            if (bar_red_or(3, 128, !ok || *abort_flag)) {
+                ok = false;
+                *abort_flag = 1;
+                break;
+            }
+            // rows >= S are not stored: the store's box is S rows high
+            if (r == 0) {
+                tma_store_2d(&to, smem_u32(ost), h * DH, b * S);
+                bulk_commit_group();
+            }
+            if (warp == WS_W_EPI && lane == 0) AWT(6, i);
         }
-        if (t == 256) bulk_wait_group0();  // every output tile written before the CTA exits
+        if (r == 0) bulk_wait_group0();  // every output tile written before the CTA exits
     }
 
     if (!ok) *abort_flag = 1;
@@ -1167,7 +1198,7 @@ k_attention_ws(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     if (*abort_flag) {
         if (t == 0) atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
         // drain: MMAs issued by the two issuing threads, TMA loads in flight
-        if (t == 32 || t == 64) {
+        if (t == 32 || t == 64 || t == 96) {
             mma_commit(bar(WB_DRAIN));
             mbar_wait(bar(WB_DRAIN), 0, nullptr, 400000000ll);
         }
