@@ -108,7 +108,10 @@ struct Cfg {
     static constexpr int RES_OFF = STAGES * STAGE + 256 + 2 * BN * 4;  // after ring, barriers, bias
     static constexpr int TAB_OFF = RES_OFF + RES_BYTES;  // the rest holds the conv tap table
     static constexpr int TAB_MAX = (SMEM - 1024 - TAB_OFF) / 4;  // tap-table entries
-    static constexpr int GROUPS = BN / 64;              // accumulator column groups of 64
+    // accumulator column groups: 64 columns per warp, or 32 when BN is not a
+    // multiple of 64 (the 96-wide tile for N = 384 at small M)
+    static constexpr int GW = BN % 64 == 0 ? 64 : 32;
+    static constexpr int GROUPS = BN / GW;
     static constexpr int NACC = 4 * GROUPS;             // accumulator warps 8 .. 8 + NACC - 1
     // GEMM epilogue: one dense 32 x 16 staging block per accumulator warp
     // (2 KB, 1024-aligned), its 16-byte chunks swizzled as TMA's 64-byte
@@ -568,9 +571,10 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         }
     } else if (warp >= W_ACC0 && warp < W_ACC0 + NACC) {
         // accumulator / epilogue warps: warp w owns TMEM lanes 32*(w%4)..+31
-        // (tile rows) and one 64-column group of the tile
+        // (tile rows) and one GW-column group of the tile
         const int q = warp & 3, grp = (warp - W_ACC0) >> 2;
-        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::ACC_COL + grp * 64;
+        constexpr int GW = G::GW;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::ACC_COL + grp * GW;
         const int rloc = q * 32 + lane;
         int drained0 = 0, drained1 = 0;  // drain groups of buffers 0 and 1 so far
         for (int tt = 0; tt < my_tiles && ok; ++tt) {
@@ -592,9 +596,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 }
                 cp_async_commit();
             }
-            float acc[64];
+            float acc[GW];
 #pragma unroll
-            for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+            for (int j = 0; j < GW; ++j) acc[j] = 0.0f;
             for (int ci = 0; ci < nch && ok; ++ci) {
                 const int cidx = tt * nch + ci, b = cidx & 1;
                 if (!chunk_group_last(ci, chunk_group_pos(ci))) continue;  // the group goes on in TMEM
@@ -603,7 +607,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 if (warp == W_ACC0 && lane == 0) GTL(512, cidx);
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < GW / 16; ++c) {
                     uint32_t rr[16];
                     tmem_ld_32x32b_x16(lane_base + b * BN + c * 16, rr);
                     tmem_ld_wait();
@@ -687,11 +691,11 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             // leaves by TMA store (tmC, 64-byte swizzle) instead of st.global
             float *stg = reinterpret_cast<float *>(smem + G::STG_OFF) + (warp - W_ACC0) * 512;
             auto sidx = [](int r, int c4) { return r * 16 + ((c4 ^ ((r >> 1) & 3)) << 2); };
-            const int rbase = m0 + q * 32, cbase = n0 + grp * 64;
-            const float *sbg = sb + grp * 64;
+            const int rbase = m0 + q * 32, cbase = n0 + grp * GW;
+            const float *sbg = sb + grp * GW;
             const bool vec = (ldc & 3) == 0 && (N & 3) == 0 && ((uintptr_t)C & 15) == 0;
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
+            for (int ch = 0; ch < GW / 16; ++ch) {
                 if (warp == W_ACC0 && lane == 0) GTL(1056, tt * 8 + 2 + ch);
                 if (cstore && lane == 0) bulk_wait_group_read0();  // the previous block has left
                 __syncwarp();
@@ -1247,23 +1251,29 @@ bool pair_enabled() {
     return on;
 }
 
-// Tile width for N: 192 or 128, by a cost model of the persistent launch:
+// Tile width for N: 192, 128 or 96, by a cost model of the persistent launch:
 // rounds of tiles over the SMs times the relative time of one tile.  A
 // 128-wide tile takes ~0.77 of a 192-wide one (its stages are MMA-issue
 // bound; measured with the widths forced on the encoder at batch 256:
 // 11.2 vs 10.1 ms per step), so the narrower tile wins only when it does not
 // add a round: e.g. N = 384 at M = 4096 (96 tiles vs 64, one round each),
-// but not at M = 8192 (192 tiles = 2 rounds vs 128 tiles = 1).  The width
+// but not at M = 8192 (192 tiles = 2 rounds vs 128 tiles = 1).  A 96-wide
+// tile (~0.6) fills one round where 128-wide ones leave SMs idle: N = 384 at
+// M = 4096 is 128 tiles for 148 SMs (FFN2 37.9 -> 33.2 us).  The width
 // does not change any output element's summation order.
 int pick_bn(int M, int N, int sms) {
     static const int forced = [] {
         const char *e = getenv("LONNX_GEMM_BN");
         return e ? atoi(e) : 0;
     }();
-    if (forced == 128 || forced == 192) return forced;
+    if (forced == 96 || forced == 128 || forced == 192) return forced;
     const int64_t rows = (M + BM - 1) / BM;
     auto rounds = [&](int bn) { return (rows * ((N + bn - 1) / bn) + sms - 1) / sms; };
-    return 0.77 * (double)rounds(128) < (double)rounds(192) ? 128 : 192;
+    // relative tile times, measured on B200: 128-wide ~0.77 and 96-wide
+    // ~0.6 of a 192-wide tile; ties go to the wider tile
+    const double c192 = (double)rounds(192), c128 = 0.77 * (double)rounds(128), c96 = 0.6 * (double)rounds(96);
+    if (c96 < c128 && c96 < c192) return 96;
+    return c128 < c192 ? 128 : 192;
 }
 
 // Conv tile width: the least padding of M among 128, 192 and 64 (ties to
@@ -1324,10 +1334,12 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
         rc = ctx_alloc(ctx, (size_t)ksplit * stride * 4, &ws);
         if (rc) return rc;
         float *w = (float *)ws;
-        rc = bn == 192 ? launch_tc<192, MODE_GEMM>(ctx, ma, mw, mwlo, nullptr, w, M, N, K, N, 1.0f, 1.0f,
+        rc = bn == 192  ? launch_tc<192, MODE_GEMM>(ctx, ma, mw, mwlo, nullptr, w, M, N, K, N, 1.0f, 1.0f,
+                                                    LONNX_EPI_NONE, none, ksplit, stride)
+             : bn == 96 ? launch_tc<96, MODE_GEMM>(ctx, ma, mw, mwlo, nullptr, w, M, N, K, N, 1.0f, 1.0f,
                                                    LONNX_EPI_NONE, none, ksplit, stride)
-                       : launch_tc<128, MODE_GEMM>(ctx, ma, mw, mwlo, nullptr, w, M, N, K, N, 1.0f, 1.0f,
-                                                   LONNX_EPI_NONE, none, ksplit, stride);
+                        : launch_tc<128, MODE_GEMM>(ctx, ma, mw, mwlo, nullptr, w, M, N, K, N, 1.0f, 1.0f,
+                                                    LONNX_EPI_NONE, none, ksplit, stride);
         if (rc == LONNX_OK) {
             int64_t blocks = (stride + 255) / 256;
             if (blocks > (int64_t)ctx->num_sms * 8) blocks = (int64_t)ctx->num_sms * 8;
@@ -1339,7 +1351,7 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
         ctx_free(ctx, ws);
         return rc;
     }
-    if (M >= 2 * BM && pair_enabled()) {
+    if (M >= 2 * BM && bn != 96 && pair_enabled()) {
         // CTA pairs (cta_group::2): each CTA loads half of the weight tile
         CUtensorMap mwp, mwlop;
         rc = make_map(&mwp, Whi, N, K, ldw, bn / 2);
@@ -1350,6 +1362,7 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
         return launch_pair<128>(ctx, ma, mwp, mwlop, bias, C, M, N, K, ldc, alpha, beta, epi);
     }
     if (bn == 192) return launch_tc<192, MODE_GEMM>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
+    if (bn == 96) return launch_tc<96, MODE_GEMM>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
     return launch_tc<128, MODE_GEMM>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
 }
 
