@@ -37,6 +37,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait with a suspend-time hint: the thread sleeps (issuing nothing)
+// until the phase completes or about `ns` nanoseconds pass
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+// mbar_wait whose polls sleep between tries (for warps that are idle while
+// they wait and would otherwise take issue slots from the warps doing work)
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, volatile int *abort,
+                                                long long limit_cycles = 4000000000ll) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (abort && *abort) return false;
+        if (clock64() - t0 > limit_cycles) return false;
+    }
+}
 // Wait for the phase of `parity` on `bar`, giving up after ~limit_cycles SM
 // clocks (default ~2 s at 2 GHz) or when another thread of the CTA raised
 // *abort.  Returns false on give-up.  The timer is the SM's cycle counter
