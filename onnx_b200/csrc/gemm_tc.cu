@@ -580,18 +580,34 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         for (int tt = 0; tt < my_tiles && ok; ++tt) {
             const int t = t0 + tt * (int)gridDim.x, n0 = tile_n0(t), m0 = tile_m0(t);
             if constexpr (RES) {
-                // this thread's residual row (its pixel, its 64 channels) into
-                // shared memory now; only this thread reads it back, after a
-                // wait on its own copy group, in the epilogue
-                const int grow = m0 + rloc;
-                if (grow < M) {
-                    const int img = grow / cv.img_rows, pix = grow - img * cv.img_rows;
-                    const float *rs = cv.res + (int64_t)img * N * cv.img_rows + pix;
-                    const uint32_t d0 = smem_u32(sres) + (uint32_t)(grp * 64 * BM + rloc) * 4;
+                // the warp's residual block (its 32 pixels x its 64 channels)
+                // into shared memory now, read back in the epilogue after a
+                // wait on the copy group and a __syncwarp.  With 4 | pixels
+                // per image, each copy is 16 bytes: 4 consecutive pixels of one
+                // channel (16 per thread; 64 four-byte copies per thread cost
+                // ~5.6k cycles of the accumulator warps' time per tile)
+                if (cv.img_rows % 4 == 0 && ((uintptr_t)cv.res & 15) == 0) {
+#pragma unroll 4
+                    for (int i = 0; i < 16; ++i) {
+                        const int f = lane + 32 * i, rg = f & 7, u = f >> 3;  // 4-pixel group, channel
+                        const int grow = m0 + q * 32 + rg * 4, col = n0 + grp * 64 + u;
+                        const bool in = grow < M && col < N;
+                        const int img = grow / cv.img_rows, pix = grow - img * cv.img_rows;
+                        const float *src = in ? cv.res + ((int64_t)img * N + col) * cv.img_rows + pix : cv.res;
+                        cp_async16(smem_u32(sres) + (uint32_t)((grp * 64 + u) * BM + q * 32 + rg * 4) * 4, src,
+                                   in ? 16u : 0u);
+                    }
+                } else {
+                    const int grow = m0 + rloc;
+                    if (grow < M) {
+                        const int img = grow / cv.img_rows, pix = grow - img * cv.img_rows;
+                        const float *rs = cv.res + (int64_t)img * N * cv.img_rows + pix;
+                        const uint32_t d0 = smem_u32(sres) + (uint32_t)(grp * 64 * BM + rloc) * 4;
 #pragma unroll 8
-                    for (int u = 0; u < 64; ++u) {
-                        const int col = n0 + grp * 64 + u;
-                        cp_async4(d0 + u * BM * 4, col < N ? rs + col * cv.img_rows : cv.res, col < N ? 4u : 0u);
+                        for (int u = 0; u < 64; ++u) {
+                            const int col = n0 + grp * 64 + u;
+                            cp_async4(d0 + u * BM * 4, col < N ? rs + col * cv.img_rows : cv.res, col < N ? 4u : 0u);
+                        }
                     }
                 }
                 cp_async_commit();
@@ -621,6 +637,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             }
             if (!ok) break;
             if constexpr (CONV) {
+                if (warp == W_ACC0 && lane == 0) GTL(1024, tt);
                 // NCHW output: row = (image, pixel), column = channel; a
                 // warp's lanes hold consecutive pixels, so each column store
                 // coalesces.  The optional residual (same layout) is added
@@ -636,6 +653,12 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                     sb[c] = bv;
                 }
                 asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
+                if constexpr (RES) {
+                    // the residual block: this thread's copies, then the
+                    // other lanes' (every lane of the warp reaches this)
+                    cp_async_wait<0>();
+                    __syncwarp();
+                }
                 const int grow = m0 + rloc;
                 if (grow < M) {
                     const int img = grow / cv.img_rows, pix = grow - img * cv.img_rows;
@@ -655,7 +678,6 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                             if (cb + u < N) dst[(cb + u) * cs] = x;
                         }
                     } else {
-                        cp_async_wait<0>();
                         const float *sr = sres + grp * 64 * BM + rloc;
 #pragma unroll
                         for (int u = 0; u < 64; ++u) {
@@ -666,6 +688,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                         }
                     }
                 }
+                if (warp == W_ACC0 && lane == 0) GTL(1040, tt);
                 continue;
             }
             if (warp == W_ACC0 && lane == 0) GTL(1024, tt);
