@@ -823,281 +823,6 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     }
 }
 
-// ---- CTA-pair GEMM (cta_group::2) ------------------------------------------
-//
-// Plain GEMM (row-major A, C) on a pair of CTAs in one cluster: the pair
-// computes a 256 x BN tile with tcgen05.mma.cta_group::2 (M = 256).  Each CTA
-// loads its own 128 rows of A and HALF of the weight tile (BN / 2 rows of W_hi
-// and W_lo) into its own shared memory, moves its A rows into its own TMEM
-// (hi / lo), and keeps its own 128 x BN accumulator rows in TMEM; the leader
-// (cluster rank 0) issues the MMAs for both.  Per SM a 32-wide stage is then
-// 16 KB of A + BN * 128 B of W instead of 16 KB + 2 * BN * 128 B, so the
-// ring holds 5-6 stages instead of 3-4: the single-CTA kernel waits on TMA
-// latency with its shallow ring, this one keeps the tensor pipe fed.
-//
-// Cross-CTA hand-offs (every load is this CTA's own, from local HBM):
-//   A rows in TMEM      both CTAs' A warps arrive on the leader's conv(s)
-//                       (the peer's remotely, release at cluster scope); an
-//                       A warp arrives only after its own full(s), so this
-//                       also covers each CTA's W half
-//   stage / A buffer /  one tcgen05.commit from the leader arrives on the
-//   chunk ready         barrier at the same offset in both CTAs
-//   chunk drained       both CTAs' accumulator warps arrive on the leader's
-//                       tdrain(b)
-// Waits are bounded like the single-CTA kernel's; on expiry the CTA raises
-// its abort flag and both CTAs still meet at the final cluster barrier.
-template <int BN>
-struct PairCfg {
-    static constexpr int WH = BN / 2;                  // weight rows per CTA
-    static constexpr int W_TILE = WH * BK * 4;
-    static constexpr int STAGE = A_TILE + 2 * W_TILE;
-    static constexpr int FIT = (227 * 1024 - 1024 - 256) / STAGE;
-    static constexpr int STAGES = FIT > 6 ? 6 : FIT;
-    static constexpr int SMEM = STAGES * STAGE + 1024 + 256;
-    static constexpr int GROUPS = BN / 64;
-    static constexpr int NACC = 4 * GROUPS;
-    static constexpr int ACC_COL = 0;
-    static constexpr int A_COL = 2 * BN;
-    static constexpr int NAB = 2 * BN + 3 * 64 <= 512 ? 3 : 2;
-    static constexpr int TMEM_COLS = 2 * BN + NAB * 64 <= 256 ? 256 : 512;
-    static_assert(3 * STAGES + 5 + NAB <= 30, "barrier area");
-    static_assert(BM * (BN + 4) * 4 + BN * 4 <= STAGES * STAGE, "C tile + bias must fit in the stage ring");
-};
-
-template <int BN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-k_gemm_pair_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
-                   const __grid_constant__ CUtensorMap tmWlo, const float *__restrict__ bias, float *__restrict__ C,
-                   int M, int N, int K, int ldc, float alpha, float beta, int epi, int *dev_flags) {
-    using G = PairCfg<BN>;
-    constexpr int S = G::STAGES, NACC = G::NACC, NAB = G::NAB;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * G::STAGE);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 5 + NAB);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_rank();
-    const bool leader = rank == 0;
-    const int nk = (K + BK - 1) / BK;
-    const int ntn = (N + BN - 1) / BN;
-    const int pair = (int)blockIdx.x >> 1;
-    const int n0 = (pair % ntn) * BN, m0 = (pair / ntn) * (2 * BM) + (int)rank * BM;
-    const int w0 = n0 + (int)rank * G::WH;  // this CTA's weight rows
-
-    auto full = [&](int s) { return smem_u32(bars + s); };
-    auto conv = [&](int s) { return smem_u32(bars + S + s); };
-    auto empty = [&](int s) { return smem_u32(bars + 2 * S + s); };
-    auto tfull = [&](int b) { return smem_u32(bars + 3 * S + b); };
-    auto tdrain = [&](int b) { return smem_u32(bars + 3 * S + 2 + b); };
-    const uint32_t drainbar = smem_u32(bars + 3 * S + 4);
-    auto afree = [&](int b) { return smem_u32(bars + 3 * S + 5 + b); };
-    auto lead = [&](uint32_t a) { return mapa_shared(a, 0u); };
-    auto stageA = [&](int s) { return smem + s * G::STAGE; };
-    auto stageW = [&](int s) { return smem + s * G::STAGE + A_TILE; };
-    auto stageWlo = [&](int s) { return smem + s * G::STAGE + A_TILE + G::W_TILE; };
-    int issued = 0;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(full(s), 1);
-            mbar_init(conv(s), 8);  // the A warps of both CTAs (leader's copy is the one used)
-            mbar_init(empty(s), 1);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(tfull(b), 1);
-            mbar_init(tdrain(b), 2 * NACC);  // the accumulator warps of both CTAs
-        }
-        for (int b = 0; b < NAB; ++b) mbar_init(afree(b), 1);
-        mbar_init(drainbar, 1);
-        *abort_flag = 0;
-        fence_mbar_init();
-        prefetch_tmap(&tmA);
-        prefetch_tmap(&tmW);
-        prefetch_tmap(&tmWlo);
-    }
-    if (warp == W_MMA) {
-        tmem_alloc_pair(smem_u32(tmem_slot), G::TMEM_COLS);
-        tmem_relinquish_pair();
-    }
-    tc_fence_before();
-    cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA traffic
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    bool ok = true;
-
-    if (warp == W_TMA) {
-        if (lane == 0) {
-            constexpr uint32_t bytes = G::STAGE;
-            for (int j = 0; j < nk && ok; ++j) {
-                const int s = j % S;
-                if (!mbar_wait(empty(s), ((j / S) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                mbar_arrive_expect_tx(full(s), bytes);
-                tma_load_2d(smem_u32(stageA(s)), &tmA, full(s), j * BK, m0);
-                tma_load_2d(smem_u32(stageW(s)), &tmW, full(s), j * BK, w0);
-                tma_load_2d(smem_u32(stageWlo(s)), &tmWlo, full(s), j * BK, w0);
-                issued = j + 1;
-            }
-        }
-    } else if (warp == W_MMA) {
-        if (leader && lane == 0) {
-            constexpr uint32_t idesc = idesc_tf32(2 * BM, BN);
-            for (int j = 0; j < nk && ok; ++j) {
-                const int s = j % S, b = j & 1, ab = j % NAB;
-                if (!mbar_wait_cluster(conv(s), (j / S) & 1, abort_flag)) { ok = false; break; }
-                if (!mbar_wait_cluster(tdrain(b), ((j >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t acc = tmem + G::ACC_COL + b * BN;
-                const uint32_t ahi = tmem + G::A_COL + ab * 64, alo = ahi + 32;
-                const uint32_t w = smem_u32(stageW(s)), wlo = smem_u32(stageWlo(s));
-#pragma unroll
-                for (int kk = 0; kk < BK / 8; ++kk) {
-                    const uint64_t dw = smem_desc_sw128(w + kk * 32), dwl = smem_desc_sw128(wlo + kk * 32);
-                    mma_tf32_ts_pair(acc, alo + kk * 8, dw, idesc, kk != 0);
-                    mma_tf32_ts_pair(acc, ahi + kk * 8, dwl, idesc, 1);
-                    mma_tf32_ts_pair(acc, ahi + kk * 8, dw, idesc, 1);
-                }
-                // one commit arrives on the barrier at this offset in both CTAs
-                mma_commit_pair_both(empty(s), 3);
-                mma_commit_pair_both(afree(ab), 3);
-                mma_commit_pair_both(tfull(b), 3);
-            }
-        }
-    } else if (warp >= W_A0 && warp < W_A0 + 4) {
-        const int q = warp & 3, r = q * 32 + lane;
-        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::A_COL;
-        for (int j = 0; j < nk && ok; ++j) {
-            const int s = j % S, b = j % NAB;
-            if (!mbar_wait(full(s), (j / S) & 1, abort_flag)) { ok = false; break; }
-            if (!mbar_wait(afree(b), ((j / NAB) & 1) ^ 1, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-            const uint8_t *row = stageA(s) + r * 128;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t hi[16], lo[16];
-#pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-                    const int c = h * 4 + c4;  // 16-byte chunk, 128B-swizzled
-                    const float4 v = *reinterpret_cast<const float4 *>(row + (((c ^ (r & 7))) << 4));
-                    const float x[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float hv = tf32_hi(x[u]);
-                        hi[c4 * 4 + u] = __float_as_uint(hv);
-                        lo[c4 * 4 + u] = __float_as_uint(__fsub_rn(x[u], hv));
-                    }
-                }
-                tmem_st_32x32b_x16(lane_base + b * 64 + h * 16, hi);
-                tmem_st_32x32b_x16(lane_base + b * 64 + 32 + h * 16, lo);
-            }
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if (leader) mbar_arrive(conv(s));
-                else mbar_arrive_cluster(lead(conv(s)));
-            }
-        }
-    } else if (warp >= W_ACC0 && warp < W_ACC0 + NACC) {
-        const int q = warp & 3, grp = (warp - W_ACC0) >> 2;
-        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::ACC_COL + grp * 64;
-        const int rloc = q * 32 + lane;
-        float acc[64];
-#pragma unroll
-        for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
-        for (int i = 0; i < nk && ok; ++i) {
-            const int b = i & 1;
-            if (!mbar_wait(tfull(b), (i >> 1) & 1, abort_flag)) { ok = false; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t rr[16];
-                tmem_ld_32x32b_x16(lane_base + b * BN + c * 16, rr);
-                tmem_ld_wait();
-#pragma unroll
-                for (int u = 0; u < 16; ++u) acc[c * 16 + u] = __fadd_rn(acc[c * 16 + u], __uint_as_float(rr[u]));
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                if (leader) mbar_arrive(tdrain(b));
-                else mbar_arrive_cluster(lead(tdrain(b)));
-            }
-        }
-        // row-major epilogue through the (now idle) ring, as in the single-CTA kernel
-        constexpr int PITCH = BN + 4;
-        float *ctile = reinterpret_cast<float *>(smem);
-        float *sbias = ctile + BM * PITCH;
-        const int tid = threadIdx.x - W_ACC0 * 32;
-        for (int c = tid; c < BN; c += NACC * 32) {
-            const int col = n0 + c;
-            float bv = 0.0f;
-            if (bias && col < N) bv = beta == 1.0f ? __ldg(bias + col) : __fmul_rn(beta, __ldg(bias + col));
-            sbias[c] = bv;
-        }
-        if (ok) {
-#pragma unroll
-            for (int j = 0; j < 64; j += 4)
-                *reinterpret_cast<float4 *>(ctile + rloc * PITCH + grp * 64 + j) =
-                    make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-        }
-        asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
-        if (ok) {
-            constexpr int V4 = BN / 4;
-            const bool vec = (ldc & 3) == 0 && n0 + BN <= N;
-#pragma unroll 1
-            for (int e = tid; e < BM * V4; e += NACC * 32) {
-                const int rr = e / V4, c4 = e % V4;
-                const int grow = m0 + rr;
-                if (grow >= M) continue;
-                const float4 raw = *reinterpret_cast<const float4 *>(ctile + rr * PITCH + c4 * 4);
-                float v[4] = {raw.x, raw.y, raw.z, raw.w};
-                const int col0 = n0 + c4 * 4;
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    float x = v[u];
-                    if (alpha != 1.0f) x = __fmul_rn(x, alpha);
-                    if (bias) x = __fadd_rn(x, sbias[c4 * 4 + u]);
-                    if (epi == LONNX_EPI_RELU) x = x > 0.0f ? x : 0.0f;
-                    else if (epi == LONNX_EPI_GELU_ERF) x = lonnx_gelu_chain(x);
-                    v[u] = x;
-                }
-                float *dst = C + (int64_t)grow * ldc + col0;
-                if (vec) {
-                    *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
-                } else {
-                    for (int u = 0; u < 4; ++u)
-                        if (col0 + u < N) dst[u] = v[u];
-                }
-            }
-        }
-    }
-
-    if (!ok) {
-        *abort_flag = 1;
-        atomicExch(dev_flags + lonnx::FLAG_TIMEOUT, 1);
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (leader && warp == W_MMA && lane == 0) {
-        // every MMA (and with them the commits to both CTAs' barriers) has
-        // completed before either CTA goes on to free TMEM or exit
-        mma_commit_pair(drainbar);
-        mbar_wait(drainbar, 0, nullptr, 400000000ll);
-    }
-    if (*abort_flag && warp == W_TMA && lane == 0) {
-        for (int j = issued - S < 0 ? 0 : issued - S; j < issued; ++j)
-            mbar_wait(full(j % S), (j / S) & 1, nullptr, 400000000ll);
-    }
-    __syncthreads();
-    cluster_sync();
-    if (warp == W_MMA) {
-        tc_fence_after();
-        tmem_dealloc_pair(tmem, G::TMEM_COLS);
-    }
-}
-
 // Weight preparation: W given as [K, N] (trans = 0) or [N, K] (trans = 1)
 // -> hi, lo as [N, K] with hi = tf32(w) (low 13 mantissa bits cleared) and
 // lo = w - hi (exact).  Run once per weight; O(N K).
@@ -1245,35 +970,6 @@ __global__ void k_splitk_reduce(const float *__restrict__ ws, int splits, int64_
     }
 }
 
-template <int BN>
-int launch_pair(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, const CUtensorMap &mwlo,
-                const float *bias, float *C, int M, int N, int K, int ldc, float alpha, float beta, int epi) {
-    using G = PairCfg<BN>;
-    static bool attr_set[64] = {false};
-    if (!attr_set[ctx->device & 63]) {
-        LONNX_CUDA(cudaFuncSetAttribute(k_gemm_pair_tf32x3<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        G::SMEM));
-        attr_set[ctx->device & 63] = true;
-    }
-    const int64_t pairs = (int64_t)((N + BN - 1) / BN) * ((M + 2 * BM - 1) / (2 * BM));
-    if (pairs >= (1ll << 30)) return lonnx::set_error(LONNX_E_UNSUPPORTED, "gemm_tc: too many tiles");
-    k_gemm_pair_tf32x3<BN><<<(unsigned)(2 * pairs), kThreads, G::SMEM, ctx->stream>>>(
-        ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, ctx->dev_flags);
-    LONNX_CHECK_LAUNCH(ctx);
-    return LONNX_OK;
-}
-
-// The pair kernel is opt-in (LONNX_GEMM_PAIR=1): measured on B200 it is
-// correct but 3-5% slower than the single-CTA kernel on the encoder and
-// sweep shapes, both settling near 1.6k SM cycles per 32-wide stage.
-bool pair_enabled() {
-    static const bool on = [] {
-        const char *e = getenv("LONNX_GEMM_PAIR");
-        return e && e[0] == '1';
-    }();
-    return on;
-}
-
 // Tile width for N: 192, 128 or 96, by a cost model of the persistent launch:
 // rounds of tiles over the SMs times the relative time of one tile.  A
 // 128-wide tile takes ~0.77 of a 192-wide one (its stages are MMA-issue
@@ -1373,16 +1069,6 @@ int gemm_tc(lonnx_ctx *ctx, const float *A, const float *Whi, const float *Wlo, 
         }
         ctx_free(ctx, ws);
         return rc;
-    }
-    if (M >= 2 * BM && bn != 96 && pair_enabled()) {
-        // CTA pairs (cta_group::2): each CTA loads half of the weight tile
-        CUtensorMap mwp, mwlop;
-        rc = make_map(&mwp, Whi, N, K, ldw, bn / 2);
-        if (rc) return rc;
-        rc = make_map(&mwlop, Wlo, N, K, ldw, bn / 2);
-        if (rc) return rc;
-        if (bn == 192) return launch_pair<192>(ctx, ma, mwp, mwlop, bias, C, M, N, K, ldc, alpha, beta, epi);
-        return launch_pair<128>(ctx, ma, mwp, mwlop, bias, C, M, N, K, ldc, alpha, beta, epi);
     }
     if (bn == 192) return launch_tc<192, MODE_GEMM>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);
     if (bn == 96) return launch_tc<96, MODE_GEMM>(ctx, ma, mw, mwlo, bias, C, M, N, K, ldc, alpha, beta, epi, none);

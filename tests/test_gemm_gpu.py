@@ -170,10 +170,13 @@ def test_gemm_split_k_epilogue(ctx, epi):
     close(got, y.astype(np.float32))
 
 
-def test_gemm_cta_pair_kernel_vs_fp64():
-    """The CTA-pair (cta_group::2) GEMM kernel, opt-in via LONNX_GEMM_PAIR=1,
-    run in a child process (the switch is read once per process) on an
-    encoder shape and a ragged one, against float64."""
+def test_gemm_96_wide_tiles_vs_fp64():
+    """The 96-wide tile (accumulator warps in 32-column groups; the tile-width
+    model picks it for N = 384 at small M), forced via LONNX_GEMM_BN=96 in a
+    child process (the switch is read once per process), on the encoder's
+    batch-32 FFN2 shape, a ragged one and a GELU epilogue, against float64;
+    and bit-identical to the 128-wide tile (the width changes no element's
+    summation order)."""
     import os
     import subprocess
     import sys
@@ -183,20 +186,35 @@ sys.path.insert(0, %r)
 from onnx_b200.tensor import Context, DeviceTensor
 from onnx_b200 import _native as N
 ctx = Context(0)
-for (M, K, N_, tb) in [(1024, 384, 1536, 1), (700, 520, 200, 0)]:
+out = []
+for (M, K, N_, tb, epi) in [(4096, 1536, 384, 0, 0), (700, 520, 200, 1, 0), (1000, 384, 96, 0, 2)]:
     rng = np.random.default_rng(M)
     A = rng.uniform(-1, 1, (M, K)).astype(np.float32)
     B = rng.uniform(-1, 1, (N_, K) if tb else (K, N_)).astype(np.float32)
     b = rng.uniform(-1, 1, N_).astype(np.float32)
     ref = A.astype(np.float64) @ (B.T if tb else B).astype(np.float64) + b
+    if epi == 2:
+        from math import erf, sqrt
+        ref = 0.5 * ref * (1 + np.vectorize(erf)(ref / sqrt(2)))
     dA, dB, db = (DeviceTensor.from_host(ctx, x) for x in (A, B, b))
     y = DeviceTensor(ctx, (M, N_), np.float32)
-    N.check(N.lib.lonnx_gemm_f32(ctx.handle, dA.ptr, dB.ptr, db.ptr, y.ptr, 1, M, N_, K, 0, 0, 0, tb, 1.0, 1.0, 0))
+    N.check(N.lib.lonnx_gemm_f32(ctx.handle, dA.ptr, dB.ptr, db.ptr, y.ptr, 1, M, N_, K, 0, 0, 0, tb, 1.0, 1.0, epi))
     ctx.sync()
-    err = np.abs(y.to_host() - ref) - (1e-4 + 1e-4 * np.abs(ref))
+    got = y.to_host()
+    err = np.abs(got - ref) - (1e-4 + 1e-4 * np.abs(ref))
     assert err.max() <= 0, (M, K, N_, float(err.max()))
+    out.append(got)
+np.save(sys.argv[1], np.concatenate([o.ravel() for o in out]))
 print("ok")
 ''' % os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, LONNX_GEMM_PAIR="1")
-    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
-    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+    import tempfile
+    import numpy as np
+    res = {}
+    with tempfile.TemporaryDirectory() as d:
+        for bn in ("96", "128"):
+            f = os.path.join(d, bn + ".npy")
+            env = dict(os.environ, LONNX_GEMM_BN=bn)
+            r = subprocess.run([sys.executable, "-c", code, f], env=env, capture_output=True, text=True, timeout=300)
+            assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+            res[bn] = np.load(f)
+    assert np.array_equal(res["96"], res["128"])
