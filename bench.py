@@ -594,14 +594,18 @@ def main():
     # faster of the two on a short untimed probe (same decision on every
     # rank: both probes are max over ranks).  Replay wins at small batches,
     # where the launches themselves cost time (batch 32: 1.42 vs 1.51 ms).
-    probe = max(3, args.warmup)
-    t_eager = timed_steps(cg.run, probe)
+    # (each probe after 10 warm steps of its own: the first steps after an
+    # idle gap run ~10% faster than the sustained rate, power-limited clocks)
+    probe = 10
     l0 = ctx.launches
     cg.capture()
     kernels_per_replay = ctx.launches - l0
-    for _ in range(args.warmup):
+    for _ in range(probe):
         cg.replay()
     t_replay = timed_steps(cg.replay, probe)
+    for _ in range(probe):
+        cg.run()
+    t_eager = timed_steps(cg.run, probe)
     use_replay = t_replay < t_eager
     step_fn = cg.replay if use_replay else cg.run
     l0 = ctx.launches
