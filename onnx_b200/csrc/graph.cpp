@@ -21,6 +21,10 @@
 //   [Add(a, b) ->] ReduceMean -> Sub -> Pow(2) -> ReduceMean -> Add(eps) ->
 //   Sqrt -> Div -> Mul(gamma) -> Add(beta)
 //       => one LayerNorm kernel (with the residual Add folded in)
+//   Conv(+Add bias)(+Relu) -> MaxPool -> ... -> Reshape -> MatMul -> Add(bias)
+//   on a batch-1 input whose activations fit in shared memory (mnist-8)
+//       => one single-CTA kernel for the whole chain (tiny.cu), bit-identical
+//          to the per-step kernels it replaces
 // A fused step re-checks its shapes at run time and otherwise executes its
 // original nodes.  flags & 2 applies Conv's strides/pads/dilations/group
 // attributes; without it Conv sees them as absent, as the reference does
@@ -125,7 +129,7 @@ struct NodeDef {
     }
 };
 
-enum StepKind { S_NODE, S_GEMM, S_LN, S_ATTN, S_CONV };
+enum StepKind { S_NODE, S_GEMM, S_LN, S_ATTN, S_CONV, S_TINY };
 
 struct Step {
     StepKind kind = S_NODE;
@@ -150,6 +154,8 @@ struct Step {
     float scale = 1;
     bool qkv_packed = false;  // q/k/v are column slices of one [T, 3H] GEMM output
     std::string qkv;
+    // TINY: a chain of steps run as one small-network kernel when it fits
+    std::vector<Step> sub;
 };
 
 }  // namespace
@@ -376,24 +382,18 @@ void exec_matmul(lonnx_graph *g, const NodeDef &n) {
 // Conv node, optionally fused: relu = a following Relu, res = the other
 // input of a following Add (same shape as the Conv output; the caller
 // checks), whi/wlo = the weight split at prepare time.
-bool exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string *out_name = nullptr,
-               const Value *res = nullptr, const float *whi = nullptr, const float *wlo = nullptr,
-               int w_tapmajor = 0, const Value *bias_add = nullptr) {
-    Value x = lookup(g, n.in.at(0)), w = lookup(g, n.in.at(1));
-    Value bias;
-    // bias_add: a following per-channel Add folded in as the bias (the conv
-    // has none); the bias pass after the sum is the Add node's one rounding
-    const bool has_bias = bias_add || (n.in.size() > 2 && !n.in[2].empty());
-    if (bias_add) bias = *bias_add;
-    else if (has_bias) bias = lookup(g, n.in[2]);
-    if (w.dtype != x.dtype) fail(LONNX_E_BADARG, "The weights tensor must be the same type as the input tensor.");
-    if (x.shape.size() != 4) fail(LONNX_E_SHAPE, "The input tensor " + n.in[0] + " for parameter X has shape " + shape_str(x.shape) + " but is required to have rank 4.");
-    if (w.shape.size() != 4) fail(LONNX_E_SHAPE, "The input tensor " + n.in[1] + " for parameter W has shape " + shape_str(w.shape) + " but is required to have rank 4.");
-    // attributes that reach the op (see file header)
+// Conv geometry from the node's attributes (as the reference's op sees them,
+// see the file header) and the input / weight shapes
+struct ConvGeom {
+    int N, C, H, W, M, kh, kw, sh, sw, pt, pl, pb, pr, dh, dw, group, Ho, Wo;
+};
+ConvGeom conv_geom(lonnx_graph *g, const NodeDef &n, const std::vector<int64_t> &xs, const std::vector<int64_t> &ws) {
+    if (xs.size() != 4) fail(LONNX_E_SHAPE, "The input tensor " + n.in[0] + " for parameter X has shape " + shape_str(xs) + " but is required to have rank 4.");
+    if (ws.size() != 4) fail(LONNX_E_SHAPE, "The input tensor " + n.in[1] + " for parameter W has shape " + shape_str(ws) + " but is required to have rank 4.");
     std::vector<int64_t> strides{1, 1}, dil{1, 1}, pads_v;
     std::vector<int64_t> *pads = nullptr;
     int group = 1;
-    int kh = (int)w.shape[2], kw = (int)w.shape[3];
+    int kh = (int)ws[2], kw = (int)ws[3];
     if (g->honor_conv_attrs) {
         if (const Attr *a = n.get("strides")) strides = a->ints;
         if (const Attr *a = n.get("dilations")) dil = a->ints;
@@ -409,33 +409,56 @@ bool exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string
         mode = 2;
         pv = (int)(*pads)[0];
     }
-    const int N = (int)x.shape[0], C = (int)x.shape[1], H = (int)x.shape[2], W = (int)x.shape[3];
-    const int M = (int)w.shape[0];
+    ConvGeom c{};
+    c.N = (int)xs[0]; c.C = (int)xs[1]; c.H = (int)xs[2]; c.W = (int)xs[3];
+    c.M = (int)ws[0]; c.kh = kh; c.kw = kw; c.group = group;
+    c.sh = (int)strides[0]; c.sw = (int)strides[1]; c.dh = (int)dil[0]; c.dw = (int)dil[1];
     const int ekh = dil[0] <= 1 ? kh : kh + (kh - 1) * ((int)dil[0] - 1);
     const int ekw = dil[1] <= 1 ? kw : kw + (kw - 1) * ((int)dil[1] - 1);
-    PadInfo p = conv_output_info(mode, H, W, (int)strides[0], (int)strides[1], ekh, ekw, pv);
+    PadInfo p = conv_output_info(mode, c.H, c.W, c.sh, c.sw, ekh, ekw, pv);
     // the reference hands (left, top, right, bottom) to MathOps.Conv2D as
     // (padY, padX, padH, padW), TensorOps.cs:937
-    const int pt = p.left, pl = p.top, pb = p.right, pr = p.bottom;
-    const int Ho = (H + pt + pb - ((int)dil[0] * (kh - 1) + 1)) / (int)strides[0] + 1;
-    const int Wo = (W + pl + pr - ((int)dil[1] * (kw - 1) + 1)) / (int)strides[1] + 1;
-    if (Ho != p.oh || Wo != p.ow) fail(LONNX_E_SHAPE, "Conv: output geometry mismatch");
+    c.pt = p.left; c.pl = p.top; c.pb = p.right; c.pr = p.bottom;
+    c.Ho = (c.H + c.pt + c.pb - (c.dh * (kh - 1) + 1)) / c.sh + 1;
+    c.Wo = (c.W + c.pl + c.pr - (c.dw * (kw - 1) + 1)) / c.sw + 1;
+    if (c.Ho != p.oh || c.Wo != p.ow) fail(LONNX_E_SHAPE, "Conv: output geometry mismatch");
+    return c;
+}
+
+// Conv node, optionally fused: relu = a following Relu, res = the other
+// input of a following Add (same shape as the Conv output; the caller
+// checks), whi/wlo = the weight split at prepare time.
+bool exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string *out_name = nullptr,
+               const Value *res = nullptr, const float *whi = nullptr, const float *wlo = nullptr,
+               int w_tapmajor = 0, const Value *bias_add = nullptr) {
+    Value x = lookup(g, n.in.at(0)), w = lookup(g, n.in.at(1));
+    Value bias;
+    // bias_add: a following per-channel Add folded in as the bias (the conv
+    // has none); the bias pass after the sum is the Add node's one rounding
+    const bool has_bias = bias_add || (n.in.size() > 2 && !n.in[2].empty());
+    if (bias_add) bias = *bias_add;
+    else if (has_bias) bias = lookup(g, n.in[2]);
+    if (w.dtype != x.dtype) fail(LONNX_E_BADARG, "The weights tensor must be the same type as the input tensor.");
+    const ConvGeom c = conv_geom(g, n, x.shape, w.shape);
     ensure_dev(g, x);
     ensure_dev(g, w);
     if (has_bias) ensure_dev(g, bias);
-    Value y = new_dev(g, DT_FLOAT, {N, M, Ho, Wo});
+    Value y = new_dev(g, DT_FLOAT, {c.N, c.M, c.Ho, c.Wo});
     if (res && res->shape != y.shape) return false;
     ck(lonnx::conv2d(g->ctx, (const float *)x.dptr(), (const float *)w.dptr(), whi, wlo,
                      has_bias ? (const float *)bias.dptr() : nullptr, res ? (const float *)res->dptr() : nullptr,
-                     (float *)y.dptr_mut(), N, C, H, W, M, kh, kw, (int)strides[0], (int)strides[1], pt, pl, pb, pr,
-                     (int)dil[0], (int)dil[1], group, relu, w_tapmajor));
+                     (float *)y.dptr_mut(), c.N, c.C, c.H, c.W, c.M, c.kh, c.kw, c.sh, c.sw, c.pt, c.pl, c.pb, c.pr,
+                     c.dh, c.dw, c.group, relu, w_tapmajor));
     g->env[out_name ? *out_name : n.out.at(0)] = y;
     return true;
 }
 
-void exec_maxpool(lonnx_graph *g, const NodeDef &n) {
-    Value x = lookup(g, n.in.at(0));
-    if (x.shape.size() != 4) fail(LONNX_E_SHAPE, "The input tensor " + n.in[0] + " for parameter X has shape " + shape_str(x.shape) + " but is required to have rank 4.");
+// MaxPool geometry: kernel, strides, pads (top, left) and the output size
+struct PoolGeom {
+    int N, C, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo;
+};
+PoolGeom pool_geom(const NodeDef &n, const std::vector<int64_t> &xs) {
+    if (xs.size() != 4) fail(LONNX_E_SHAPE, "The input tensor " + n.in[0] + " for parameter X has shape " + shape_str(xs) + " but is required to have rank 4.");
     const Attr *ks = n.get("kernel_shape");
     if (!ks) fail(LONNX_E_BADARG, "kernelshape");
     std::vector<int64_t> strides = ks->ints, dil{1, 1}, pads_v;
@@ -445,15 +468,24 @@ void exec_maxpool(lonnx_graph *g, const NodeDef &n) {
     if (const Attr *a = n.get("pads")) { pads_v = a->ints; pads = &pads_v; }
     int pv = 0;
     const int mode = pad_mode(n, pads, &pv);
-    const int N = (int)x.shape[0], C = (int)x.shape[1], H = (int)x.shape[2], W = (int)x.shape[3];
-    const int kh = (int)ks->ints[0], kw = (int)ks->ints[1];
-    const int ekh = dil[0] <= 1 ? kh : kh + (kh - 1) * ((int)dil[0] - 1);
-    const int ekw = dil[1] <= 1 ? kw : kw + (kw - 1) * ((int)dil[1] - 1);
-    PadInfo p = conv_output_info(mode, H, W, (int)strides[0], (int)strides[1], ekh, ekw, pv);
+    PoolGeom q{};
+    q.N = (int)xs[0]; q.C = (int)xs[1]; q.H = (int)xs[2]; q.W = (int)xs[3];
+    q.kh = (int)ks->ints[0]; q.kw = (int)ks->ints[1];
+    q.sh = (int)strides[0]; q.sw = (int)strides[1];
+    const int ekh = dil[0] <= 1 ? q.kh : q.kh + (q.kh - 1) * ((int)dil[0] - 1);
+    const int ekw = dil[1] <= 1 ? q.kw : q.kw + (q.kw - 1) * ((int)dil[1] - 1);
+    PadInfo p = conv_output_info(mode, q.H, q.W, q.sh, q.sw, ekh, ekw, pv);
+    q.pt = p.top; q.pl = p.left; q.Ho = p.oh; q.Wo = p.ow;
+    return q;
+}
+
+void exec_maxpool(lonnx_graph *g, const NodeDef &n) {
+    Value x = lookup(g, n.in.at(0));
+    const PoolGeom q = pool_geom(n, x.shape);
     ensure_dev(g, x);
-    Value y = new_dev(g, DT_FLOAT, {N, C, p.oh, p.ow});
-    ck(lonnx_maxpool2d_f32(g->ctx, (const float *)x.dptr(), (float *)y.dptr_mut(), N, C, H, W, kh, kw, (int)strides[0],
-                           (int)strides[1], p.top, p.left, p.oh, p.ow));
+    Value y = new_dev(g, DT_FLOAT, {q.N, q.C, q.Ho, q.Wo});
+    ck(lonnx_maxpool2d_f32(g->ctx, (const float *)x.dptr(), (float *)y.dptr_mut(), q.N, q.C, q.H, q.W, q.kh, q.kw, q.sh,
+                           q.sw, q.pt, q.pl, q.Ho, q.Wo));
     g->env[n.out.at(0)] = y;
 }
 
@@ -590,10 +622,13 @@ void exec_transpose(lonnx_graph *g, const NodeDef &n) {
     g->env[n.out.at(0)] = y;
 }
 
-void exec_reshape(lonnx_graph *g, const NodeDef &n) {
-    Value x = lookup(g, n.in.at(0));
+// Reshape's output shape for an input of shape xs (0 copies a dimension
+// unless allowzero, one -1 is inferred)
+std::vector<int64_t> reshape_shape(lonnx_graph *g, const NodeDef &n, const std::vector<int64_t> &xs) {
     std::vector<int64_t> shp = ints_of(g, n.in.at(1));
     const bool allow_zero = n.get("allowzero") && n.get("allowzero")->i;
+    int64_t numel = 1;
+    for (auto d : xs) numel *= d;
     int unknown = -1;
     int64_t known = 1;
     std::vector<int64_t> out;
@@ -604,21 +639,26 @@ void exec_reshape(lonnx_graph *g, const NodeDef &n) {
             unknown = (int)i;
             out.push_back(-1);
         } else if (shp[i] == 0 && !allow_zero) {
-            out.push_back(x.shape.at(i));
-            known *= x.shape[i];
+            out.push_back(xs.at(i));
+            known *= xs[i];
         } else {
             out.push_back(shp[i]);
             known *= shp[i];
         }
     }
-    if (unknown >= 0) out[unknown] = known ? x.numel() / known : 0;
+    if (unknown >= 0) out[unknown] = known ? numel / known : 0;
     int64_t tot = 1;
     for (auto d : out) tot *= d;
-    if (tot != x.numel())
-        fail(LONNX_E_SHAPE, "The input tensor cannot be reshaped to the requested shape. Input shape:" + shape_str(x.shape) +
+    if (tot != numel)
+        fail(LONNX_E_SHAPE, "The input tensor cannot be reshaped to the requested shape. Input shape:" + shape_str(xs) +
                                 ", requested shape:" + shape_str(out));
+    return out;
+}
+
+void exec_reshape(lonnx_graph *g, const NodeDef &n) {
+    Value x = lookup(g, n.in.at(0));
     Value y = x;  // zero-copy view
-    y.shape = out;
+    y.shape = reshape_shape(g, n, x.shape);
     g->env[n.out.at(0)] = y;
 }
 
@@ -1645,24 +1685,188 @@ void build_steps(lonnx_graph *g, bool fuse) {
             g->steps.push_back(s);
         }
     }
+    // small-network chains: consecutive Conv / MaxPool / Reshape / MatMul /
+    // Add steps starting at a Conv, each taking the previous step's output,
+    // which nothing else uses, as its input.  Whether a chain runs as one
+    // kernel is decided at run time (batch 1, sizes; exec_tiny_step).
+    auto out_of = [&](const Step &st) -> std::string {
+        if (st.kind == S_CONV) return st.y;
+        if (st.kind == S_NODE && st.nodes.size() == 1 && !g->nodes[st.nodes[0]].out.empty())
+            return g->nodes[st.nodes[0]].out[0];
+        return std::string();
+    };
+    auto chain_op = [&](const Step &st) {
+        if (st.kind == S_CONV) return true;
+        if (st.kind != S_NODE || st.nodes.size() != 1) return false;
+        const std::string &op = g->nodes[st.nodes[0]].op;
+        return op == "MaxPool" || op == "Reshape" || op == "MatMul" || op == "Add";
+    };
+    auto takes = [&](const Step &st, const std::string &prev) {
+        if (prev.empty()) return false;
+        const int cons = m.only_consumer(prev);  // -1 as well for a graph output
+        if (cons < 0 || std::find(st.nodes.begin(), st.nodes.end(), cons) == st.nodes.end()) return false;
+        if (st.kind == S_CONV) return g->nodes[st.nodes[0]].in.at(0) == prev;
+        const NodeDef &nd = g->nodes[st.nodes[0]];
+        if (nd.op == "Add") return nd.in.size() == 2 && ((nd.in[0] == prev) != (nd.in[1] == prev));
+        return !nd.in.empty() && nd.in[0] == prev;
+    };
+    std::vector<Step> chained;
+    for (size_t i = 0; i < g->steps.size();) {
+        size_t j = i + 1;
+        if (g->steps[i].kind == S_CONV)
+            while (j < g->steps.size() && chain_op(g->steps[j]) && takes(g->steps[j], out_of(g->steps[j - 1]))) ++j;
+        if (j - i >= 3) {
+            Step t;
+            t.kind = S_TINY;
+            for (size_t k = i; k < j; ++k) {
+                t.sub.push_back(g->steps[k]);
+                for (int x : g->steps[k].nodes) t.nodes.push_back(x);
+            }
+            chained.push_back(t);
+        } else {
+            for (size_t k = i; k < j; ++k) chained.push_back(g->steps[k]);
+        }
+        i = j;
+    }
+    g->steps.swap(chained);
+}
+
+// The chain of a TINY step as one kernel, planned from the run-time shapes;
+// false (nothing run) when a step of it would not take the per-step kernels
+// that tiny.cu reproduces, or an activation does not fit.
+bool exec_tiny_step(lonnx_graph *g, const Step &s) {
+    static const bool off = getenv("LONNX_TINY_CHAIN") && getenv("LONNX_TINY_CHAIN")[0] == '0';
+    if (off || s.sub.empty() || s.sub[0].kind != S_CONV) return false;
+    const NodeDef &c0 = g->nodes[s.sub[0].nodes[0]];
+    Value x = lookup(g, c0.in.at(0));
+    if (x.dtype != DT_FLOAT || x.shape.size() != 4 || x.shape[0] != 1) return false;
+    TinyProg p{};
+    std::vector<int64_t> cur = x.shape;
+    auto numel = [](const std::vector<int64_t> &v) {
+        int64_t n = 1;
+        for (auto d : v) n *= d;
+        return n;
+    };
+    p.in_elems = (int)std::min<int64_t>(numel(cur), 1 << 30);
+    if (numel(cur) > TINY_MAX_SMEM_FLOATS) return false;
+    int64_t maxe = numel(cur);
+    std::vector<Value> keep;  // device buffers the kernel reads
+    std::string prev;         // the previous sub-step's output
+    for (const Step &st : s.sub) {
+        if (p.n >= TINY_MAX_LAYERS) return false;
+        TinyLayer &L = p.L[p.n];
+        if (st.kind == S_CONV) {
+            const NodeDef &c = g->nodes[st.nodes[0]];
+            Value w = lookup(g, c.in.at(1));
+            if (w.dtype != DT_FLOAT) return false;
+            const ConvGeom q = conv_geom(g, c, cur, w.shape);
+            const int64_t total = (int64_t)q.N * q.M * q.Ho * q.Wo, K = (int64_t)q.C * q.kh * q.kw;
+            if (q.N != 1 || q.group != 1 || total * K >= gemm_tc_min_work()) return false;  // not the direct kernel
+            Value bias;
+            bool has_bias = c.in.size() > 2 && !c.in[2].empty();
+            if (!st.b.empty()) {  // the Add after the conv: a per-channel bias only (no residual)
+                if (has_bias) return false;
+                bias = lookup(g, st.b);
+                if (bias.dtype != DT_FLOAT || !channel_bias_shape(bias, q.M)) return false;
+                has_bias = true;
+            } else if (has_bias) {
+                bias = lookup(g, c.in[2]);
+                if (bias.dtype != DT_FLOAT || bias.numel() != q.M) return false;
+            }
+            ensure_dev(g, w);
+            if (has_bias) ensure_dev(g, bias);
+            keep.push_back(w);
+            if (has_bias) keep.push_back(bias);
+            L = TinyLayer{TINY_CONV, q.C, q.H, q.W, q.M, q.kh, q.kw, q.sh, q.sw, q.pt, q.pl, q.dh, q.dw, q.Ho, q.Wo,
+                          st.epi ? 1 : 0, 0, 0, (const float *)w.dptr(), has_bias ? (const float *)bias.dptr() : nullptr};
+            cur = {1, q.M, q.Ho, q.Wo};
+        } else if (st.kind == S_NODE && st.nodes.size() == 1) {
+            const NodeDef &n = g->nodes[st.nodes[0]];
+            if (n.op == "MaxPool") {
+                const PoolGeom q = pool_geom(n, cur);
+                L = TinyLayer{TINY_MAXPOOL, q.C, q.H, q.W, 0, q.kh, q.kw, q.sh, q.sw, q.pt, q.pl, 1, 1, q.Ho, q.Wo,
+                              0, 0, 0, nullptr, nullptr};
+                cur = {1, q.C, q.Ho, q.Wo};
+            } else if (n.op == "Reshape") {
+                cur = reshape_shape(g, n, cur);
+                L = TinyLayer{};
+                L.op = TINY_VIEW;
+            } else if (n.op == "MatMul") {
+                Value w = lookup(g, n.in.at(1));
+                if (w.dtype != DT_FLOAT || w.shape.size() != 2 || cur.size() != 2 || cur[0] != 1 || cur[1] != w.shape[0])
+                    return false;
+                const int64_t K = w.shape[0], N = w.shape[1];
+                // the path the product would take: below the tensor-core
+                // threshold and small enough for k_gemm_rowdot_smem
+                if (K * N >= gemm_tc_min_work() || N > 256 || (K + K * N) * 4 > 48 * 1024) return false;
+                ensure_dev(g, w);
+                keep.push_back(w);
+                L = TinyLayer{};
+                L.op = TINY_FC;
+                L.K = (int)K;
+                L.N = (int)N;
+                L.w = (const float *)w.dptr();
+                cur = {1, N};
+            } else if (n.op == "Add") {
+                // the bias Add right after the MatMul
+                if (p.n == 0 || p.L[p.n - 1].op != TINY_FC || p.L[p.n - 1].bias) return false;
+                Value b = lookup(g, n.in.at(0) == prev ? n.in.at(1) : n.in.at(0));
+                const int64_t N = p.L[p.n - 1].N;
+                if (b.dtype != DT_FLOAT || b.numel() != N || b.shape.size() > 2 || b.shape.back() != N) return false;
+                ensure_dev(g, b);
+                keep.push_back(b);
+                p.L[p.n - 1].bias = (const float *)b.dptr();
+                prev = n.out.at(0);
+                continue;  // folded into the MatMul layer
+            } else {
+                return false;
+            }
+        } else {
+            return false;
+        }
+        prev = st.kind == S_CONV ? st.y : g->nodes[st.nodes[0]].out.at(0);
+        ++p.n;
+        maxe = std::max(maxe, numel(cur));
+    }
+    if (p.n == 0) return false;
+    p.max_elems = (int)std::min<int64_t>(maxe, 1 << 30);
+    int64_t smem = 2 * maxe;  // two activation buffers, then every layer's weights
+    for (int l = 0; l < p.n; ++l) {
+        TinyLayer &L = p.L[l];
+        L.woff = (int)std::min<int64_t>(smem, 1 << 30);
+        smem += L.op == TINY_FC ? (int64_t)L.K * L.N : L.op == TINY_CONV ? (int64_t)L.M * L.C * L.kh * L.kw : 0;
+    }
+    if (smem > TINY_MAX_SMEM_FLOATS) return false;
+    p.smem_floats = (int)smem;
+    ensure_dev(g, x);
+    Value y = new_dev(g, DT_FLOAT, cur);
+    ck(tiny_chain(g->ctx, p, (const float *)x.dptr(), (float *)y.dptr_mut()));
+    const Step &last = s.sub.back();
+    g->env[last.kind == S_CONV ? last.y : g->nodes[last.nodes[0]].out.at(0)] = y;
+    return true;
+}
+
+void run_step(lonnx_graph *g, const Step &s) {
+    bool done = false;
+    switch (s.kind) {
+    case S_GEMM: done = exec_gemm_step(g, s); break;
+    case S_LN: done = exec_ln_step(g, s); break;
+    case S_ATTN: done = exec_attn_step(g, s); break;
+    case S_CONV: done = exec_conv_step(g, s); break;
+    case S_TINY:
+        if (!exec_tiny_step(g, s))
+            for (const Step &t : s.sub) run_step(g, t);
+        return;
+    default: break;
+    }
+    if (!done) {
+        if (s.kind == S_ATTN && s.qkv_packed) fail(LONNX_E_SHAPE, "fused attention: unexpected shapes for packed QKV");
+        for (int i : s.nodes) exec_node(g, g->nodes[i]);
+    }
 }
 
 void run_steps(lonnx_graph *g) {
-    for (auto &s : g->steps) {
-        bool done = false;
-        switch (s.kind) {
-        case S_GEMM: done = exec_gemm_step(g, s); break;
-        case S_LN: done = exec_ln_step(g, s); break;
-        case S_ATTN: done = exec_attn_step(g, s); break;
-        case S_CONV: done = exec_conv_step(g, s); break;
-        default: break;
-        }
-        if (!done) {
-            if (s.kind == S_ATTN && s.qkv_packed)
-                fail(LONNX_E_SHAPE, "fused attention: unexpected shapes for packed QKV");
-            for (int i : s.nodes) exec_node(g, g->nodes[i]);
-        }
-    }
+    for (auto &s : g->steps) run_step(g, s);
 }
 
 template <typename F>

@@ -103,6 +103,24 @@ struct ConvArgs {
     int tab = 0;  // set by conv_tc: the per-CTA tap table fits (see gemm_tc.cu)
     int nhwc = 0; // x is NHWC and the weights are tap-major: K order (ky, kx, c)
 };
+// A small batch-1 network run as one launch on a cluster of CTAs (tiny.cu):
+// a chain of layers; every CTA holds all weights and the current activation
+// in shared memory (2 * max_elems + the weights <= TINY_MAX_SMEM_FLOATS).
+enum { TINY_CONV = 0, TINY_MAXPOOL = 1, TINY_FC = 2, TINY_VIEW = 3 };
+constexpr int TINY_MAX_LAYERS = 12;
+constexpr int TINY_MAX_SMEM_FLOATS = 48 * 1024;
+struct TinyLayer {
+    int op;
+    int C, H, W, M, kh, kw, sh, sw, pt, pl, dh, dw, Ho, Wo, relu;  // conv / pool (pool: C planes)
+    int K, N;                                                      // fc
+    const float *w, *bias;
+    int woff;  // the weights' offset from the start of shared memory (floats), past both activation buffers
+};
+struct TinyProg {
+    int n, in_elems, max_elems, smem_floats;
+    TinyLayer L[TINY_MAX_LAYERS];
+};
+int tiny_chain(lonnx_ctx *ctx, const TinyProg &p, const float *x, float *y);
 // Convs gathered from an NHWC copy of their input (one tap's 32 consecutive
 // channels per K stage, 16-byte copies) with tap-major weights: C a multiple
 // of 32 and a kernel of 2..63 taps.
