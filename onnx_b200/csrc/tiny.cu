@@ -23,6 +23,9 @@ namespace {
 using lonnx::TinyLayer;
 using lonnx::TinyProg;
 
+// Phase marks of CTA 0 (clock64: start, set-up done, each layer done),
+// compiled only into a diagnostic build (-DLONNX_TINY_TIMELINE); read back
+// with lonnx_debug_tiny_timeline.
 #ifdef LONNX_TINY_TIMELINE
 __device__ long long g_tiny_tl[64];
 #define TTL(i)                                                                  \
