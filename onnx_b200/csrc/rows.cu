@@ -288,6 +288,62 @@ __global__ void k_maxpool2d(const float *__restrict__ x, float *__restrict__ y, 
     }
 }
 
+// MaxPool 3x3 / stride 2 / pad (1, 1) with W % 4 == 0 and Wo == W / 2 (the
+// ResNet stem's pool).  A thread computes two adjacent outputs (columns 2j,
+// 2j + 1) for RS consecutive output rows: input row r contributes the
+// float4 x[r][4j .. 4j + 3] plus column 4j - 1, the left neighbour lane's .w
+// through a shuffle (an explicit load on lane 0; -inf at j = 0, the pad).
+// Each input row of the strip is loaded once, as 16 bytes, and all 2 RS + 1
+// loads are issued before the first max.  The per-output scalar kernel
+// issues 9 four-byte loads per output, each warp access spanning three
+// 128-byte lines: L1-wavefront bound at ~69% of HBM.  Same maxima, so the
+// same bits (fmaxf from -inf over the clipped window, any order).
+template <int RS>
+__global__ void __launch_bounds__(256) k_maxpool3s2(const float *__restrict__ x, float *__restrict__ y,
+                                                    int64_t total, int H, int W, int Ho, int Wo, int strips) {
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool active = g < total;
+    const int P = W >> 2;                                 // column pairs per output row
+    const int64_t per_plane = (int64_t)P * strips;
+    const int64_t plane = active ? g / per_plane : 0;
+    const int t = active ? (int)(g - plane * per_plane) : 0;
+    const int s = t / P, j = t - s * P, lane = threadIdx.x & 31;
+    const int oy0 = s * RS, rin0 = 2 * oy0 - 1;
+    const float *xp = x + plane * H * W + 4 * j;
+    constexpr int NR = 2 * RS + 1;
+    float4 v[NR];
+    float h[NR];
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+        const int r = rin0 + i;
+        const bool in = active && r >= 0 && r < H;
+        v[i] = in ? __ldg(reinterpret_cast<const float4 *>(xp + (int64_t)r * W))
+                  : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        h[i] = in && j > 0 && lane == 0 ? __ldg(xp + (int64_t)r * W - 1) : -INFINITY;
+    }
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+        const float w = __shfl_up_sync(0xffffffffu, v[i].w, 1);
+        if (j > 0 && lane > 0) h[i] = w;  // lane - 1 holds column pair j - 1 of the same strip
+    }
+    float a[NR], b[NR];  // row maxima for output columns 2j and 2j + 1
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+        a[i] = fmaxf(fmaxf(h[i], v[i].x), v[i].y);
+        b[i] = fmaxf(fmaxf(v[i].y, v[i].z), v[i].w);
+    }
+    if (!active) return;
+    float *yp = y + plane * Ho * Wo + 2 * j;
+#pragma unroll
+    for (int o = 0; o < RS; ++o) {
+        const int oy = oy0 + o;
+        if (oy >= Ho) break;
+        const float2 r2 = make_float2(fmaxf(fmaxf(a[2 * o], a[2 * o + 1]), a[2 * o + 2]),
+                                      fmaxf(fmaxf(b[2 * o], b[2 * o + 1]), b[2 * o + 2]));
+        *reinterpret_cast<float2 *>(yp + (int64_t)oy * Wo) = r2;
+    }
+}
+
 }  // namespace
 
 using namespace lonnx;
@@ -408,6 +464,15 @@ LONNX_API int lonnx_maxpool2d_f32(lonnx_ctx *ctx, const float *x, float *y, int 
     if ((int64_t)H * W >= ((int64_t)1 << 31) || (int64_t)Ho * Wo >= ((int64_t)1 << 31))
         return set_error(LONNX_E_UNSUPPORTED, "maxpool: plane of more than 2^31 elements");
     const int64_t planes = (int64_t)N * C;
+    if (kh == 3 && kw == 3 && sh == 2 && sw == 2 && pt == 1 && pl == 1 && W % 4 == 0 && Wo == W / 2 &&
+        Ho <= (H + 2) / 2 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 7) == 0) {
+        constexpr int RS = 4;
+        const int strips = (Ho + RS - 1) / RS;
+        const int64_t tot = planes * (W / 4) * strips;
+        k_maxpool3s2<RS><<<(unsigned)((tot + 255) / 256), 256, 0, ctx->stream>>>(x, y, tot, H, W, Ho, Wo, strips);
+        LONNX_CHECK_LAUNCH(ctx);
+        return LONNX_OK;
+    }
     const int per_plane = Ho * Wo;
     // about 16 blocks per SM in all; each thread then walks several planes
     const int64_t bx = (per_plane + 255) / 256;

@@ -260,6 +260,23 @@ def test_maxpool_many_planes_and_resnet_shape(P):
                                          strides=[2, 2]))
 
 
+@pytest.mark.parametrize("xs,pads", [((2, 3, 9, 12), [1, 1, 1, 1]), ((1, 70, 20, 40), [1, 1, 1, 1]),
+                                     ((3, 5, 16, 16), [1, 1, 1, 1]), ((1, 1, 4, 4), [1, 1, 1, 1]),
+                                     ((2, 33, 7, 20), [1, 1, 1, 1])])
+def test_maxpool_3x3_s2_strip_kernel(P, xs, pads):
+    """The 3x3 / stride-2 / pad-1 strip kernel (W % 4 == 0, Wo == W / 2):
+    odd heights, output heights that are not a multiple of the strip, column
+    pairs that do not divide a warp (halo loads on lane 0, warps spanning
+    strips and planes), ReLU zeros and infinities; bit-exact."""
+    rng = np.random.default_rng(sum(xs))
+    x = np.maximum(rng.standard_normal(xs), 0).astype(np.float32)
+    x.flat[::97] = np.inf
+    x.flat[5::89] = -np.inf
+    got = ok(P.MaxPool(x, auto_pad="NOTSET", kernel_shape=[3, 3], pads=pads, strides=[2, 2]))
+    ref = O.maxpool(x, auto_pad="NOTSET", kernel_shape=[3, 3], pads=pads, strides=[2, 2])
+    assert np.array_equal(got, ref)
+
+
 def test_gelu_unary_matches_node_chain(ctx):
     """The fused Erf-GELU (lonnx_unary_f32 op 4) against the exported node
     chain Div(sqrt 2) -> Erf -> Add(1) -> Mul(x) -> Mul(0.5) on the oracle,
