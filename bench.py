@@ -451,6 +451,94 @@ def resnet_throughput(ctx, st, torch, batch=64, reps=5):
             "tflops_algorithmic": round(fl * batch / (ms * 1e-3) / 1e12, 2)}
 
 
+def resnet_conv_classes(ctx, st, torch, batch=64, reps=5):
+    """Every distinct Conv of resnet50() at batch 64 x 224^2 -- (C, M, H,
+    k, stride) and its epilogue (bias, bias + Relu, or bias + residual Add +
+    Relu, as the fusion pass runs it in the network) -- timed alone through
+    the executor (CUDA events, warm, inputs > L2 for every class but the
+    smallest), with its count in the network, TFLOP/s and tensor-pipe
+    fraction (3 x of dense tf32; 3xTF32 issues 3 MMAs per product)."""
+    from onnx_b200 import graphs as G
+    from onnx_b200.graph import ComputationalGraph
+    from onnx_b200.graphs import GraphDef, Node
+    from onnx_b200.tensor import DeviceTensor
+    _, bf16, kind = peaks()
+    tf32_peak = bf16 / 2.0
+    g = G.resnet50(seed=0)
+    consumers = {}
+    for n in g.nodes:
+        for i in n.inputs:
+            consumers.setdefault(i, []).append(n)
+    shapes = {"data": (3, 224, 224)}
+    classes, fused_adds = {}, set()
+    for n in g.nodes:
+        if n.op == "MaxPool":
+            c, h, w = shapes[n.inputs[0]]
+            shapes[n.outputs[0]] = (c, (h + 2 - 3) // 2 + 1, (w + 2 - 3) // 2 + 1)
+            continue
+        if n.op in ("Relu", "Add"):
+            if n.inputs[0] in shapes:
+                shapes[n.outputs[0]] = shapes[n.inputs[0]]
+            continue
+        if n.op != "Conv":
+            continue
+        c, h, _ = shapes[n.inputs[0]]
+        m = g.initializers[n.inputs[1]].shape[0]
+        k, s, p = n.attrs["kernel_shape"][0], n.attrs["strides"][0], n.attrs["pads"][0]
+        ho = (h + 2 * p - k) // s + 1
+        shapes[n.outputs[0]] = (m, ho, ho)
+        nxt = consumers.get(n.outputs[0], [])
+        epi = "relu" if [u.op for u in nxt] == ["Relu"] else "bias"
+        if [u.op for u in nxt] == ["Add"] and id(nxt[0]) not in fused_adds:
+            # the fusion pass claims Conv -> Add -> Relu for the first conv (in
+            # node order) that feeds the Add; the other input conv (a projection
+            # shortcut) runs with its bias only
+            fused_adds.add(id(nxt[0]))
+            epi = "add+relu"
+        key = (c, m, h, k, s, p, epi)
+        classes[key] = classes.get(key, 0) + 1
+    rng = np.random.default_rng(0)
+    out, total_us = [], 0.0
+    for (c, m, h, k, s, p, epi), count in classes.items():
+        ho = (h + 2 * p - k) // s + 1
+        attrs = {"kernel_shape": [k, k], "strides": [s, s], "pads": [p] * 4, "auto_pad": "NOTSET", "group": 1,
+                 "dilations": [1, 1]}
+        inits = {"w": (rng.standard_normal((m, c, k, k)) * np.sqrt(2.0 / (c * k * k))).astype(np.float32),
+                 "b": (rng.standard_normal(m) * 0.01).astype(np.float32)}
+        nodes = [Node("Conv", ["x", "w", "b"], ["y"], attrs)]
+        ins = ["x"]
+        last = "y"
+        if epi == "relu":
+            nodes.append(Node("Relu", ["y"], ["z"]))
+            last = "z"
+        elif epi == "add+relu":
+            nodes += [Node("Add", ["y", "r"], ["sum"]), Node("Relu", ["sum"], ["z"])]
+            ins.append("r")
+            last = "z"
+        cg = ComputationalGraph(GraphDef(nodes, inits, ins, [last]), ctx, honor_conv_attrs=True)
+        feed = {"x": DeviceTensor.from_host(ctx, rng.uniform(0, 1, (batch, c, h, h)).astype(np.float32))}
+        if epi == "add+relu":
+            feed["r"] = DeviceTensor.from_host(ctx, rng.uniform(0, 1, (batch, m, ho, ho)).astype(np.float32))
+        cg.set_inputs(feed)
+        for _ in range(2):
+            cg.run()
+        ctx.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            cg.run()
+        e1.record(st)
+        e1.synchronize()
+        us = e0.elapsed_time(e1) / reps * 1e3
+        tf = 2.0 * batch * ho * ho * m * c * k * k / (us * 1e-6) / 1e12
+        total_us += us * count
+        out.append({"conv": f"{c}->{m} {k}x{k}/{s} at {h}^2", "epilogue": epi, "count": count, "us": round(us, 1),
+                    "tflops": round(tf, 1), "tensor_pipe_frac": round(3 * tf / tf32_peak, 3)})
+    del cg, feed
+    return {"batch": batch, "peak_tf32": tf32_peak, "peak_note": f"dense tf32 = {kind} bf16 / 2",
+            "sum_count_x_us": round(total_us, 1), "classes": out}
+
+
 def conv_case(ctx, st, torch, spec, reps=5):
     """One Conv (N,C,H,M,k,stride; pad k//2, bias, ReLU) through the C-ABI,
     CUDA-event timed; for profiler captures of the implicit-GEMM conv."""
@@ -502,6 +590,8 @@ def main():
                     help="run only the bandwidth-kernel sweep at 1/4 size and exit (for ncu captures)")
     ap.add_argument("--bw-only", action="store_true",
                     help="print only the full-size bandwidth-kernel sweep and exit")
+    ap.add_argument("--conv-classes", action="store_true",
+                    help="print only the ResNet-50 per-conv-class table and exit")
     ap.add_argument("--profile-case", type=int, default=0, metavar="B",
                     help="run two 2-layer e5 forwards at batch B and exit (small case for ncu captures)")
     args = ap.parse_args()
@@ -513,6 +603,12 @@ def main():
         ctx = Context(0)
         spec = [int(v) for v in args.conv_case.split(",")]
         print(json.dumps(conv_case(ctx, torch.cuda.ExternalStream(ctx.stream), torch, spec)))
+        return
+    if args.conv_classes:
+        import torch
+        from onnx_b200.tensor import Context
+        ctx = Context(0)
+        print(json.dumps(resnet_conv_classes(ctx, torch.cuda.ExternalStream(ctx.stream), torch)))
         return
     if args.resnet_case:
         import torch
@@ -651,6 +747,8 @@ def main():
     b32 = e5_batch(ctx, st, torch, cg, args.vocab) if rank == 0 else None
     mnist = mnist_latency(ctx, st, torch) if rank == 0 else None
     resnet = resnet_throughput(ctx, st, torch) if rank == 0 and not args.no_resnet else None
+    if resnet is not None:
+        resnet["conv_classes"] = resnet_conv_classes(ctx, st, torch)
     bw = bandwidth_kernels(ctx, st, torch) if rank == 0 else None
     clocks = clk.summary()
     if rank == 0:
