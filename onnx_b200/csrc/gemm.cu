@@ -8,6 +8,7 @@
 // (src/Lokad.Onnx.Tensors/MathOps.cs:380-410) -- bit-identical results on the
 // small shapes where launch latency, not the tensor pipe, is the bound.
 #include <vector>
+#include <cstdio>
 
 #include "lonnx_internal.cuh"
 
@@ -437,14 +438,37 @@ int split_rows_tapmajor(lonnx_ctx *ctx, const float *w, float *hi, float *lo, in
     return LONNX_OK;
 }
 
-bool conv_nhwc_ok(int C, int kh, int kw) {
+bool conv_nhwc_ok(int C, int kh, int kw, bool x_nhwc) {
     static const bool off = getenv("LONNX_CONV_NCHW_GATHER") != nullptr;
-    return !off && C % 32 == 0 && kh * kw > 1 && kh * kw <= 63;
+    return !off && C % 32 == 0 && (kh * kw > 1 || x_nhwc) && kh * kw <= 63;
+}
+
+// LONNX_CONV_TRACE=1: one stderr line per conv with its layouts and path
+static bool conv_trace() {
+    static const bool on = getenv("LONNX_CONV_TRACE") && getenv("LONNX_CONV_TRACE")[0] == '1';
+    return on;
+}
+
+// [N, C, H, W] <-> [N, H, W, C] copy of a float tensor into scratch
+static int relayout(lonnx_ctx *ctx, const float *x, int N, int C, int H, int W, bool to_nhwc, void **out) {
+    int rc = ctx_alloc(ctx, (size_t)N * C * H * W * 4, out);
+    if (rc) return rc;
+    const int64_t nchw[4] = {N, C, H, W}, nhwc[4] = {N, H, W, C};
+    const int64_t to[4] = {0, 2, 3, 1}, back[4] = {0, 3, 1, 2};
+    rc = transpose_launch(ctx, x, 4, to_nhwc ? nchw : nhwc, 4, to_nhwc ? to : back, *out);
+    if (rc) {
+        ctx_free(ctx, *out);
+        *out = nullptr;
+    }
+    return rc;
 }
 
 int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, const float *wlo, const float *bias,
            const float *res, float *y, int N, int C, int H, int W, int M, int kh, int kw, int sh, int sw, int pt,
-           int pl, int pb, int pr, int dh, int dw, int group, int relu, int w_tapmajor) {
+           int pl, int pb, int pr, int dh, int dw, int group, int relu, int w_tapmajor, int x_nhwc, int res_nhwc,
+           int *out_nhwc) {
+    const bool want_out = out_nhwc && *out_nhwc;
+    if (out_nhwc) *out_nhwc = 0;
     if (!x || !w || !y || N < 0 || C <= 0 || M <= 0 || kh <= 0 || kw <= 0 || sh <= 0 || sw <= 0 ||
         dh <= 0 || dw <= 0 || group <= 0 || C % group || M % group)
         return set_error(LONNX_E_BADARG, "conv2d: bad arguments");
@@ -461,53 +485,90 @@ int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, con
         // implicit GEMM on the tensor cores: rows = output pixels (N*Ho*Wo),
         // columns = output channels, contraction over (c, ky, kx) in the
         // reference's im2col order; input gathered inside the kernel, bias,
-        // residual and ReLU in the epilogue, NCHW written directly
-        // NHWC gather: the input transposed once into scratch, the weights
-        // in tap-major column order (prepared that way, or split so here)
-        const bool nhwc = conv_nhwc_ok(C, kh, kw) && (int64_t)C * H * W < (1ll << 31);
-        const int ldk = (K + 3) & ~3;
-        void *wt = nullptr, *xt = nullptr;
-        if (!whi || !wlo || (bool)w_tapmajor != nhwc) {
-            int rc = ctx_alloc(ctx, (size_t)2 * M * ldk * 4, &wt);
-            if (rc) return rc;
-            whi = (const float *)wt;
-            wlo = whi + (size_t)M * ldk;
-            rc = nhwc ? split_rows_tapmajor(ctx, w, (float *)whi, (float *)wlo, M, C, kh * kw)
-                      : split_pad_rows(ctx, w, (float *)whi, (float *)wlo, M, K, ldk);
-            if (rc) { ctx_free(ctx, wt); return rc; }
-        }
-        if (nhwc) {
-            int rc = ctx_alloc(ctx, (size_t)N * C * H * W * 4, &xt);
-            if (!rc) {
-                const int64_t shp[4] = {N, C, H, W}, perm[4] = {0, 2, 3, 1};
-                rc = transpose_launch(ctx, x, 4, shp, 4, perm, xt);
-            }
-            if (rc) {
-                if (xt) ctx_free(ctx, xt);
+        // residual and ReLU in the epilogue, NCHW (or NHWC) written directly.
+        // NHWC gather: from the NHWC input as given, or from a transposed
+        // copy in scratch, with the weights in tap-major column order
+        // (prepared that way, or split so here)
+        const bool nhwc = conv_nhwc_ok(C, kh, kw, x_nhwc) && (int64_t)C * H * W < (1ll << 31);
+        // an NHWC output of a residual conv reads its input NHWC (no tap
+        // table); a tile shape that refuses the NHWC output runs once more
+        // with an NCHW output rather than on the direct kernel
+        const bool onhwc_first = want_out && (!res || nhwc);
+        for (int attempt = 0; attempt < (onhwc_first ? 2 : 1); ++attempt) {
+            const bool onhwc = onhwc_first && attempt == 0;
+            const int ldk = (K + 3) & ~3;
+            void *wt = nullptr, *xt = nullptr, *rt = nullptr;
+            auto release = [&]() {
                 if (wt) ctx_free(ctx, wt);
-                return rc;
-            }
+                if (xt) ctx_free(ctx, xt);
+                if (rt) ctx_free(ctx, rt);
+                wt = xt = rt = nullptr;
+            };
+            // one tap: tap-major and channel-major columns are the same order
+            if (!whi || !wlo || ((bool)w_tapmajor != nhwc && kh * kw > 1)) {
+                int rc = ctx_alloc(ctx, (size_t)2 * M * ldk * 4, &wt);
+                if (rc) return rc;
+                whi = (const float *)wt;
+                wlo = whi + (size_t)M * ldk;
+                rc = nhwc ? split_rows_tapmajor(ctx, w, (float *)whi, (float *)wlo, M, C, kh * kw)
+                          : split_pad_rows(ctx, w, (float *)whi, (float *)wlo, M, K, ldk);
+                if (rc) { release(); return rc; }
+        }
+        if (nhwc != (bool)x_nhwc) {
+            const int rc = relayout(ctx, x, N, C, H, W, nhwc, &xt);
+            if (rc) { release(); return rc; }
+        }
+        if (res && onhwc != (bool)res_nhwc) {
+            const int rc = relayout(ctx, res, N, M, Ho, Wo, onhwc, &rt);
+            if (rc) { release(); return rc; }
         }
         ConvArgs cv;
-        cv.x = nhwc ? (const float *)xt : x;
+        cv.x = xt ? (const float *)xt : x;
         cv.nhwc = nhwc ? 1 : 0;
+        cv.out_nhwc = onhwc ? 1 : 0;
         cv.C = C; cv.H = H; cv.W = W; cv.kh = kh; cv.kw = kw; cv.sh = sh; cv.sw = sw;
         cv.pt = pt; cv.pl = pl; cv.dh = dh; cv.dw = dw; cv.Ho = Ho; cv.Wo = Wo;
         cv.img_rows = Ho * Wo;
-        cv.res = res;
+        cv.res = rt ? (const float *)rt : res;
         int rc = conv_tc(ctx, cv, whi, wlo, ldk, bias, y, (int)P, M, K, relu ? LONNX_EPI_RELU : LONNX_EPI_NONE);
-        if (wt) ctx_free(ctx, wt);
-        if (xt) ctx_free(ctx, xt);
+        release();
+        if (conv_trace())
+            fprintf(stderr, "[lonnx conv] N%d C%d %dx%d M%d k%dx%d s%d x_nhwc %d gather_nhwc %d out_nhwc %d res %d/%d: %s\n",
+                    N, C, H, W, M, kh, kw, sh, x_nhwc, (int)nhwc, (int)onhwc, res != nullptr, res_nhwc,
+                    rc == LONNX_OK ? "tensor cores" : rc == LONNX_E_UNSUPPORTED ? "unsupported" : "error");
+        if (rc == LONNX_OK && out_nhwc) *out_nhwc = onhwc ? 1 : 0;
         if (rc != LONNX_E_UNSUPPORTED) return rc;
+        }
+    }
+    // direct conv: NCHW in and out
+    if (conv_trace())
+        fprintf(stderr, "[lonnx conv] N%d C%d %dx%d M%d k%dx%d s%d x_nhwc %d res %d/%d: direct\n", N, C, H, W, M, kh,
+                kw, sh, x_nhwc, res != nullptr, res_nhwc);
+    void *xt = nullptr, *rt = nullptr;
+    if (x_nhwc) {
+        const int rc = relayout(ctx, x, N, C, H, W, false, &xt);
+        if (rc) return rc;
+        x = (const float *)xt;
+    }
+    if (res && res_nhwc) {
+        const int rc = relayout(ctx, res, N, M, Ho, Wo, false, &rt);
+        if (rc) { if (xt) ctx_free(ctx, xt); return rc; }
+        res = (const float *)rt;
     }
     k_conv2d_direct<<<grid_for(ctx, total), 256, 0, ctx->stream>>>(x, w, bias, y, N, C, H, W, M, kh, kw, sh, sw, pt,
                                                                      pl, dh, dw, group, Ho, Wo, res ? 0 : relu);
-    LONNX_CHECK_LAUNCH(ctx);
-    if (res) {
+    ctx->launches++;
+    cudaError_t e = cudaGetLastError();
+    int rc = e == cudaSuccess ? LONNX_OK : cuda_error(e, "kernel launch");
+    if (rc == LONNX_OK && res) {
         k_add_relu<<<grid_for(ctx, total), 256, 0, ctx->stream>>>(y, res, total, relu);
-        LONNX_CHECK_LAUNCH(ctx);
+        ctx->launches++;
+        e = cudaGetLastError();
+        rc = e == cudaSuccess ? LONNX_OK : cuda_error(e, "kernel launch");
     }
-    return LONNX_OK;
+    if (xt) ctx_free(ctx, xt);
+    if (rt) ctx_free(ctx, rt);
+    return rc;
 }
 
 }  // namespace lonnx

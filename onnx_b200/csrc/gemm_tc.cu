@@ -46,9 +46,10 @@ constexpr int A_TILE = BM * BK * 4;     // 16 KB
 constexpr int kThreads = 640;           // 20 warps
 // warp roles: 0 TMA, 1-2 MMA (1 owns TMEM), 4-7 A -> TMEM, 8-19 accumulate/epilogue
 constexpr int W_TMA = 0, W_MMA = 1, W_MMA2 = 2, W_A0 = 4, W_ACC0 = 8;
-// kernel modes: plain GEMM (A by TMA, row-major C, one tile per CTA);
-// implicit conv (A gathered, NCHW C, persistent); implicit conv + residual
-constexpr int MODE_GEMM = 0, MODE_CONV = 1, MODE_CONV_RES = 2;
+// kernel modes: plain GEMM (A by TMA, row-major C); implicit conv (A
+// gathered, NCHW C); implicit conv + residual; the two conv modes with an
+// NHWC output (row-major C = [pixels, channels], the GEMM epilogue)
+constexpr int MODE_GEMM = 0, MODE_CONV = 1, MODE_CONV_RES = 2, MODE_CONV_NHWC = 3, MODE_CONV_RES_NHWC = 4;
 // K stages per accumulator chunk.  The tensor core accumulates a chunk
 // (CH x 32 K-columns) into TMEM, rounding toward zero; the accumulator warps
 // add chunk sums into fp32 registers with round-to-nearest.  Two 32-wide
@@ -129,6 +130,14 @@ struct Cfg {
     static constexpr int NAB = 2 * BN + 3 * 64 <= 512 ? 3 : 2;
     static constexpr int TMEM_COLS = 2 * BN + NAB * 64 <= 256 ? 256 : 512;
     static_assert(3 * STAGES + 5 + NAB <= 30, "barrier area");
+    // RES with an NHWC output: the residual tile held as the epilogue's
+    // 32 x 16 staging blocks (accumulator warp w, column block ch at block
+    // w * GW / 16 + ch), TMA-loaded, finished in place and TMA-stored; one
+    // mbarrier per accumulator warp after the TMEM slot
+    static constexpr int RESB_OFF = (RES_OFF + 1023) & ~1023;
+    static constexpr int RBAR = 3 * STAGES + 6 + NAB;
+    static_assert(!RES || RESB_OFF + RES_BYTES <= SMEM - 1024, "residual blocks must fit");
+    static_assert(!RES || RBAR + NACC <= 32, "barrier area");
     static_assert(RES || GEMM_SMEM <= SMEM, "GEMM epilogue staging must fit beside the ring");
 };
 
@@ -172,7 +181,8 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
               const float *__restrict__ bias, float *__restrict__ C, int M, int N, int K, int ldc, float alpha,
               float beta, int epi, int *dev_flags, const lonnx::ConvArgs cv, int ksplit, int64_t split_stride,
               int cstore) {
-    constexpr bool CONV = MODE != MODE_GEMM, RES = MODE == MODE_CONV_RES;
+    constexpr bool CONV = MODE != MODE_GEMM, RES = MODE == MODE_CONV_RES || MODE == MODE_CONV_RES_NHWC;
+    constexpr bool OUTN = MODE == MODE_CONV_NHWC || MODE == MODE_CONV_RES_NHWC;  // conv with NHWC output
     using G = Cfg<BN, RES>;
     constexpr int S = G::STAGES;
     constexpr int NACC = G::NACC, NAG = G::NAG, NAB = G::NAB;
@@ -187,6 +197,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     float *ebias = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(bars) + 256);  // [2][BN], NCHW epilogue
     uint32_t *tab = reinterpret_cast<uint32_t *>(smem + G::TAB_OFF);                      // conv tap table
     float *sres = reinterpret_cast<float *>(smem + G::RES_OFF);  // [BN][BM] residual tile (RES)
+    float *sresb = reinterpret_cast<float *>(smem + G::RESB_OFF);  // residual blocks (RES, NHWC output)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nk_all = (K + BK - 1) / BK;
@@ -227,6 +238,9 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
     auto tdrain = [&](int b) { return smem_u32(bars + 3 * S + 2 + b); };
     const uint32_t drainbar = smem_u32(bars + 3 * S + 4);
     auto afree = [&](int b) { return smem_u32(bars + 3 * S + 5 + b); };
+    auto rbar = [&](int w) { return smem_u32(bars + G::RBAR + w); };
+    // GEMM epilogue staging: past the tap table in the conv modes (NHWC output)
+    const int stg_off = !CONV ? G::STG_OFF : ((G::TAB_OFF + (cv.tab ? nk_all * BK * 4 : 0) + 1023) & ~1023);
     auto stageA = [&](int s) { return smem + s * G::STAGE; };
     auto stageW = [&](int s) { return smem + s * G::STAGE + A_TILE; };
     auto stageWlo = [&](int s) { return smem + s * G::STAGE + A_TILE + G::W_TILE; };
@@ -245,9 +259,11 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         }
         for (int b = 0; b < NAB; ++b) mbar_init(afree(b), 1);
         mbar_init(drainbar, 2);  // one commit per issuing thread
+        if constexpr (RES && OUTN)
+            for (int w = 0; w < NACC; ++w) mbar_init(rbar(w), 1);
         *abort_flag = 0;
         fence_mbar_init();
-        if constexpr (!CONV) prefetch_tmap(&tmA);
+        if constexpr (!CONV || (RES && OUTN)) prefetch_tmap(&tmA);  // A, or the residual (RES, NHWC)
         prefetch_tmap(&tmW);
         prefetch_tmap(&tmWlo);
     }
@@ -575,11 +591,27 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
         const int q = warp & 3, grp = (warp - W_ACC0) >> 2;
         constexpr int GW = G::GW;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + G::ACC_COL + grp * GW;
-        const int rloc = q * 32 + lane;
+        const int rloc = q * 32 + lane, wi = warp - W_ACC0;
         int drained0 = 0, drained1 = 0;  // drain groups of buffers 0 and 1 so far
+        bool rpend = false;              // residual blocks in flight (RES, NHWC output)
+        int rpar = 0;
         for (int tt = 0; tt < my_tiles && ok; ++tt) {
             const int t = t0 + tt * (int)gridDim.x, n0 = tile_n0(t), m0 = tile_m0(t);
-            if constexpr (RES) {
+            if constexpr (RES && OUTN) {
+                // the warp's residual rows x columns as GW / 16 blocks of 32 x 16,
+                // by TMA, once this warp's stores of the previous tile have read
+                // the blocks; landed long before the epilogue needs them
+                if (lane == 0) {
+                    bulk_wait_group_read0();
+                    mbar_arrive_expect_tx(rbar(wi), (GW / 16) * 2048);
+#pragma unroll
+                    for (int ch = 0; ch < GW / 16; ++ch)
+                        tma_load_2d(smem_u32(sresb + (wi * (GW / 16) + ch) * 512), &tmA, rbar(wi),
+                                    n0 + grp * GW + ch * 16, m0 + q * 32);
+                    rpend = true;
+                    rpar = tt & 1;
+                }
+            } else if constexpr (RES) {
                 // the warp's residual block (its 32 pixels x its 64 channels)
                 // into shared memory now, read back in the epilogue after a
                 // wait on the copy group and a __syncwarp.  With 4 | pixels
@@ -636,7 +668,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                 if (warp == W_ACC0 && lane == 0) GTL(768, cidx);
             }
             if (!ok) break;
-            if constexpr (CONV) {
+            if constexpr (CONV && !OUTN) {
                 if (warp == W_ACC0 && lane == 0) GTL(1024, tt);
                 // NCHW output: row = (image, pixel), column = channel; a
                 // warp's lanes hold consecutive pixels, so each column store
@@ -710,19 +742,59 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             if (warp == W_ACC0 && lane == 0) GTL(1056, tt * 8);
             asm volatile("bar.sync 1, %0;" ::"n"(NACC * 32) : "memory");
             if (warp == W_ACC0 && lane == 0) GTL(1056, tt * 8 + 1);
-            // 32 x 16 staging block of this warp; cstore: the finished block
-            // leaves by TMA store (tmC, 64-byte swizzle) instead of st.global
-            float *stg = reinterpret_cast<float *>(smem + G::STG_OFF) + (warp - W_ACC0) * 512;
             auto sidx = [](int r, int c4) { return r * 16 + ((c4 ^ ((r >> 1) & 3)) << 2); };
             const int rbase = m0 + q * 32, cbase = n0 + grp * GW;
             const float *sbg = sb + grp * GW;
+            if constexpr (RES && OUTN) {
+                // residual conv, NHWC output: lane = row; alpha, bias (zero
+                // where there is none), the residual and the activation in the
+                // order of the NCHW epilogue, written over the residual block,
+                // which then leaves by TMA store
+                if (lane == 0) {
+                    if (!mbar_wait(rbar(wi), rpar, abort_flag)) ok = false;
+                    rpend = false;
+                }
+                ok = __shfl_sync(0xffffffffu, (int)ok, 0) != 0;
+                if (!ok) break;
+                const bool relu = epi == LONNX_EPI_RELU;
+#pragma unroll
+                for (int ch = 0; ch < GW / 16; ++ch) {
+                    float *blk = sresb + (wi * (GW / 16) + ch) * 512;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float4 b4 = *reinterpret_cast<const float4 *>(sbg + ch * 16 + 4 * u);  // broadcast
+                        const float4 r4 = *reinterpret_cast<const float4 *>(blk + sidx(lane, u));
+                        const float bb[4] = {b4.x, b4.y, b4.z, b4.w}, rv[4] = {r4.x, r4.y, r4.z, r4.w};
+                        float v[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            float x = __fadd_rn(__fmul_rn(acc[ch * 16 + 4 * u + k], alpha), bb[k]);
+                            x = __fadd_rn(x, rv[k]);
+                            v[k] = (relu && !(x > 0.0f)) ? 0.0f : x;
+                        }
+                        *reinterpret_cast<float4 *>(blk + sidx(lane, u)) = make_float4(v[0], v[1], v[2], v[3]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && cbase + ch * 16 < N) {
+                        tma_store_2d(&tmC, smem_u32(blk), cbase + ch * 16, rbase);
+                        bulk_commit_group();
+                    }
+                }
+                if (warp == W_ACC0 && lane == 0) GTL(1040, tt);
+                continue;
+            }
+            // 32 x 16 staging block of this warp; cstore: the finished block
+            // leaves by TMA store (tmC, 64-byte swizzle) instead of st.global
+            float *stg = reinterpret_cast<float *>(smem + stg_off) + (warp - W_ACC0) * 512;
             const bool vec = (ldc & 3) == 0 && (N & 3) == 0 && ((uintptr_t)C & 15) == 0;
 #pragma unroll
             for (int ch = 0; ch < GW / 16; ++ch) {
                 if (warp == W_ACC0 && lane == 0) GTL(1056, tt * 8 + 2 + ch);
                 if (cstore && lane == 0) bulk_wait_group_read0();  // the previous block has left
                 __syncwarp();
-                if (cstore && epi != LONNX_EPI_GELU_ERF) {
+                // (a conv with an NHWC output always stores by TMA and has no GELU)
+                if (OUTN || (cstore && epi != LONNX_EPI_GELU_ERF)) {
                     // lane = row: alpha, the column's bias (the same for every
                     // lane) and Relu straight on the accumulators, then the
                     // finished block goes out by TMA -- no read-back
@@ -736,7 +808,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                         for (int k = 0; k < 4; ++k) {
                             float x = acc[ch * 16 + 4 * u + k];
                             if (alpha != 1.0f) x = __fmul_rn(x, alpha);
-                            if (bias) x = __fadd_rn(x, bb[k]);
+                            if (bias || CONV) x = __fadd_rn(x, bb[k]);
                             v[k] = (relu && !(x > 0.0f)) ? 0.0f : x;
                         }
                         *reinterpret_cast<float4 *>(stg + sidx(lane, u)) = make_float4(v[0], v[1], v[2], v[3]);
@@ -749,6 +821,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                     }
                     continue;
                 }
+                if constexpr (OUTN) continue;
 #pragma unroll
                 for (int u = 0; u < 4; ++u)
                     *reinterpret_cast<float4 *>(stg + sidx(lane, u)) = make_float4(
@@ -766,7 +839,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
                     for (int u = 0; u < 4; ++u) {
                         float x = v[u];
                         if (alpha != 1.0f) x = __fmul_rn(x, alpha);
-                        if (bias) x = __fadd_rn(x, sbg[ch * 16 + c4 + u]);
+                        if (bias || CONV) x = __fadd_rn(x, sbg[ch * 16 + c4 + u]);
                         if (epi == LONNX_EPI_RELU) x = x > 0.0f ? x : 0.0f;
                         else if (epi == LONNX_EPI_GELU_ERF) x = lonnx_gelu_fast(x);
                         v[u] = x;
@@ -796,6 +869,7 @@ k_gemm_tf32x3(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ C
             if (warp == W_ACC0 && lane == 0) GTL(1040, tt);
         }
         if (cstore && lane == 0) bulk_wait_group0();  // every block stored before the CTA exits
+        if (RES && OUTN && lane == 0 && rpend) mbar_wait(rbar(wi), rpar, nullptr, 400000000ll);  // loads in flight
     }
 
     if (!ok) {
@@ -928,12 +1002,16 @@ int launch_tc(lonnx_ctx *ctx, const CUtensorMap &ma, const CUtensorMap &mw, cons
               const lonnx::ConvArgs &cv, int ksplit = 1, int64_t split_stride = 0) {
     CUtensorMap mc = mw;  // unused unless cstore
     int cstore = 0;
-    if (MODE == MODE_GEMM && ksplit == 1 && tma_store_enabled() && (ldc & 3) == 0 && ((uintptr_t)C & 15) == 0) {
+    // (the residual conv with an NHWC output always stores by TMA: its
+    // epilogue finishes the tile in the TMA-loaded residual blocks)
+    if (((MODE == MODE_GEMM && ksplit == 1 && tma_store_enabled()) || MODE == MODE_CONV_NHWC ||
+         MODE == MODE_CONV_RES_NHWC) &&
+        (ldc & 3) == 0 && ((uintptr_t)C & 15) == 0) {
         const int rc = make_map(&mc, C, M, N, ldc, 32, 1);
         if (rc) return rc;
         cstore = 1;
     }
-    using G = Cfg<BN, MODE == MODE_CONV_RES>;
+    using G = Cfg<BN, MODE == MODE_CONV_RES || MODE == MODE_CONV_RES_NHWC>;
     static bool attr_set[64] = {false};
     if (!attr_set[ctx->device & 63]) {
         LONNX_CUDA(cudaFuncSetAttribute(k_gemm_tf32x3<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1089,7 +1167,15 @@ int conv_tc(lonnx_ctx *ctx, const ConvArgs &cv, const float *Whi, const float *W
     const int tab_max = bn == 192 ? Cfg<192>::TAB_MAX
                         : bn == 64 ? (res ? Cfg<64, true>::TAB_MAX : Cfg<64>::TAB_MAX)
                                    : (res ? Cfg<128, true>::TAB_MAX : Cfg<128>::TAB_MAX);
-    a.tab = !cv.nhwc && kend <= tab_max && cv.kh * cv.kw <= 63 && (int64_t)cv.C * cv.H * cv.W < (1ll << 24);
+    if (cv.out_nhwc && ((M & 3) || !al16(y) || (res && (!cv.nhwc || !al16(cv.res)))))
+        return set_error(LONNX_E_UNSUPPORTED, "conv_tc: NHWC output needs M %% 4 == 0, aligned y / res, NHWC x");
+    // NHWC output without a residual: the GEMM epilogue's staging blocks sit
+    // past the tap table (1024-aligned)
+    const int nacc = bn == 192 ? Cfg<192>::NACC : bn == 64 ? Cfg<64>::NACC : Cfg<128>::NACC;
+    const int stg_bytes = cv.out_nhwc && !res ? nacc * 2048 + 1024 : 0;
+    if (stg_bytes > tab_max * 4) return set_error(LONNX_E_UNSUPPORTED, "conv_tc: no room for the epilogue staging");
+    a.tab = !cv.nhwc && kend * 4 + stg_bytes <= tab_max * 4 && cv.kh * cv.kw <= 63 &&
+            (int64_t)cv.C * cv.H * cv.W < (1ll << 24);
     if (cv.nhwc && (cv.C % BK || cv.kh * cv.kw > 63 || K != cv.C * cv.kh * cv.kw))
         return set_error(LONNX_E_UNSUPPORTED, "conv_tc: NHWC gather needs C % 32 == 0 and <= 63 taps");
     CUtensorMap mw, mwlo;
@@ -1097,10 +1183,26 @@ int conv_tc(lonnx_ctx *ctx, const ConvArgs &cv, const float *Whi, const float *W
     if (rc) return rc;
     rc = make_map(&mwlo, Wlo, M, K, ldw, bn);
     if (rc) return rc;
-    // the A map is unused in implicit mode (the kernel gathers A itself)
+    // the A map is unused in implicit mode (the kernel gathers A itself); the
+    // residual conv with an NHWC output passes the residual's map there
     if (res) {
-        if (bn == 64) return launch_tc<64, MODE_CONV_RES>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
-        return launch_tc<128, MODE_CONV_RES>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+        CUtensorMap mr = mw;
+        if (a.out_nhwc) {
+            rc = make_map(&mr, cv.res, P, M, M, 32, 1);
+            if (rc) return rc;
+        }
+        if (a.out_nhwc) {
+            if (bn == 64)
+                return launch_tc<64, MODE_CONV_RES_NHWC>(ctx, mr, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+            return launch_tc<128, MODE_CONV_RES_NHWC>(ctx, mr, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+        }
+        if (bn == 64) return launch_tc<64, MODE_CONV_RES>(ctx, mr, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+        return launch_tc<128, MODE_CONV_RES>(ctx, mr, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+    }
+    if (a.out_nhwc) {
+        if (bn == 192) return launch_tc<192, MODE_CONV_NHWC>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+        if (bn == 64) return launch_tc<64, MODE_CONV_NHWC>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
+        return launch_tc<128, MODE_CONV_NHWC>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
     }
     if (bn == 192) return launch_tc<192, MODE_CONV>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);
     if (bn == 64) return launch_tc<64, MODE_CONV>(ctx, mw, mw, mwlo, bias, y, P, M, K, M, 1.0f, 1.0f, epi, a);

@@ -89,6 +89,10 @@ struct Value {
     std::shared_ptr<DevBuf> buf;     // device storage (may be shared by views)
     const void *ext = nullptr;       // caller-owned device pointer
     std::shared_ptr<std::vector<uint8_t>> host;  // host copy (int64 / small constants)
+    // device storage is [N, H, W, C] while `shape` stays the logical
+    // [N, C, H, W]: a conv-chain value (mark_nhwc); lookup() hands readers
+    // that do not ask for it an NCHW copy
+    bool nhwc = false;
     int64_t numel() const {
         int64_t n = 1;
         for (auto s : shape) n *= s;
@@ -175,6 +179,7 @@ struct lonnx_graph {
     std::map<std::string, Value> captured_outputs;
     bool honor_conv_attrs = false;
     int opset = 13;
+    std::set<std::string> nhwc_vals;  // values allowed to be stored NHWC (mark_nhwc)
 };
 
 namespace {
@@ -182,14 +187,41 @@ namespace {
 // ---------------------------------------------------------------------------
 // helpers
 
+Value new_dev(lonnx_graph *g, int dtype, const std::vector<int64_t> &shape);
+
+// An NCHW copy of an NHWC-stored value
+Value to_nchw(lonnx_graph *g, const Value &v) {
+    Value y = new_dev(g, v.dtype, v.shape);
+    const int64_t phys[4] = {v.shape[0], v.shape[2], v.shape[3], v.shape[1]}, perm[4] = {0, 3, 1, 2};
+    ck(transpose_launch(g->ctx, v.dptr(), (int)dtype_size(v.dtype), phys, 4, perm, y.dptr_mut()));
+    return y;
+}
+
+// The value as its readers expect it (NCHW): an NHWC-stored value is
+// replaced by its NCHW copy the first time a reader that does not handle
+// NHWC asks for it.
 const Value &lookup(lonnx_graph *g, const std::string &name) {
     auto it = g->env.find(name);
-    if (it != g->env.end()) return it->second;
+    if (it != g->env.end()) {
+        if (it->second.nhwc) {
+            static const bool trace = getenv("LONNX_CONV_TRACE") && getenv("LONNX_CONV_TRACE")[0] == '1';
+            if (trace) fprintf(stderr, "[lonnx conv] %s: NHWC -> NCHW for a reader\n", name.c_str());
+            it->second = to_nchw(g, it->second);
+        }
+        return it->second;
+    }
     auto ii = g->inputs.find(name);
     if (ii != g->inputs.end()) return ii->second;
     auto in = g->inits.find(name);
     if (in != g->inits.end()) return in->second;
     fail(LONNX_E_BADARG, "The required input parameter " + name + " is missing or null.");
+}
+
+// The value as stored, for the readers that handle both layouts (check .nhwc)
+const Value &lookup_raw(lonnx_graph *g, const std::string &name) {
+    auto it = g->env.find(name);
+    if (it != g->env.end()) return it->second;
+    return lookup(g, name);
 }
 
 bool has_value(lonnx_graph *g, const std::string &name) {
@@ -431,7 +463,7 @@ ConvGeom conv_geom(lonnx_graph *g, const NodeDef &n, const std::vector<int64_t> 
 bool exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string *out_name = nullptr,
                const Value *res = nullptr, const float *whi = nullptr, const float *wlo = nullptr,
                int w_tapmajor = 0, const Value *bias_add = nullptr) {
-    Value x = lookup(g, n.in.at(0)), w = lookup(g, n.in.at(1));
+    Value x = lookup_raw(g, n.in.at(0)), w = lookup(g, n.in.at(1));
     Value bias;
     // bias_add: a following per-channel Add folded in as the bias (the conv
     // has none); the bias pass after the sum is the Add node's one rounding
@@ -445,11 +477,14 @@ bool exec_conv(lonnx_graph *g, const NodeDef &n, int relu = 0, const std::string
     if (has_bias) ensure_dev(g, bias);
     Value y = new_dev(g, DT_FLOAT, {c.N, c.M, c.Ho, c.Wo});
     if (res && res->shape != y.shape) return false;
+    const std::string &oname = out_name ? *out_name : n.out.at(0);
+    int out_nhwc = g->nhwc_vals.count(oname) ? 1 : 0;  // asked for; conv2d says what it wrote
     ck(lonnx::conv2d(g->ctx, (const float *)x.dptr(), (const float *)w.dptr(), whi, wlo,
                      has_bias ? (const float *)bias.dptr() : nullptr, res ? (const float *)res->dptr() : nullptr,
                      (float *)y.dptr_mut(), c.N, c.C, c.H, c.W, c.M, c.kh, c.kw, c.sh, c.sw, c.pt, c.pl, c.pb, c.pr,
-                     c.dh, c.dw, c.group, relu, w_tapmajor));
-    g->env[out_name ? *out_name : n.out.at(0)] = y;
+                     c.dh, c.dw, c.group, relu, w_tapmajor, x.nhwc ? 1 : 0, res && res->nhwc ? 1 : 0, &out_nhwc));
+    y.nhwc = out_nhwc != 0;
+    g->env[oname] = y;
     return true;
 }
 
@@ -480,10 +515,18 @@ PoolGeom pool_geom(const NodeDef &n, const std::vector<int64_t> &xs) {
 }
 
 void exec_maxpool(lonnx_graph *g, const NodeDef &n) {
-    Value x = lookup(g, n.in.at(0));
+    Value x = lookup_raw(g, n.in.at(0));
+    if (x.nhwc && !g->nhwc_vals.count(n.out.at(0))) x = lookup(g, n.in.at(0));
     const PoolGeom q = pool_geom(n, x.shape);
     ensure_dev(g, x);
     Value y = new_dev(g, DT_FLOAT, {q.N, q.C, q.Ho, q.Wo});
+    if (x.nhwc) {  // NHWC in, NHWC out
+        ck(lonnx::maxpool2d_nhwc(g->ctx, (const float *)x.dptr(), (float *)y.dptr_mut(), q.N, q.C, q.H, q.W, q.kh,
+                                 q.kw, q.sh, q.sw, q.pt, q.pl, q.Ho, q.Wo));
+        y.nhwc = true;
+        g->env[n.out.at(0)] = y;
+        return;
+    }
     ck(lonnx_maxpool2d_f32(g->ctx, (const float *)x.dptr(), (float *)y.dptr_mut(), q.N, q.C, q.H, q.W, q.kh, q.kw, q.sh,
                            q.sw, q.pt, q.pl, q.Ho, q.Wo));
     g->env[n.out.at(0)] = y;
@@ -500,7 +543,7 @@ std::vector<int64_t> reduce_axes(lonnx_graph *g, const NodeDef &n, bool axes_fro
 }
 
 void exec_reduce(lonnx_graph *g, const NodeDef &n) {
-    Value x = lookup(g, n.in.at(0));
+    Value x = lookup_raw(g, n.in.at(0));
     if (x.dtype != DT_FLOAT) fail(LONNX_E_UNSUPPORTED, "The operation " + n.op + " is not supported by the backend.");
     const bool attr_axes = (n.op == "ReduceMean" && g->opset < 13);
     std::vector<int64_t> axes = reduce_axes(g, n, attr_axes);
@@ -514,6 +557,18 @@ void exec_reduce(lonnx_graph *g, const NodeDef &n) {
         if (!red[d]) oshape.push_back(x.shape[d]);
         else if (keep) oshape.push_back(1);
     const int op = n.op == "ReduceSum" ? LONNX_REDUCE_SUM : n.op == "ReduceMax" ? LONNX_REDUCE_MAX : LONNX_REDUCE_MEAN;
+    if (x.nhwc) {
+        if (rank == 4 && !red[0] && !red[1] && red[2] && red[3]) {
+            // over H x W of an NHWC value: [N, H*W, C] -> [N, C], the same
+            // bits as the NCHW reduction (k_reduce_hw_nhwc)
+            Value y = new_dev(g, DT_FLOAT, oshape);
+            ck(lonnx::reduce_hw_nhwc(g->ctx, op, (const float *)x.dptr(), (float *)y.dptr_mut(), (int)x.shape[0],
+                                     (int)(x.shape[2] * x.shape[3]), (int)x.shape[1]));
+            g->env[n.out.at(0)] = y;
+            return;
+        }
+        x = lookup(g, n.in.at(0));
+    }
     ensure_dev(g, x);
     Value y = new_dev(g, DT_FLOAT, oshape);
     ck(lonnx_reduce_f32(g->ctx, op, (const float *)x.dptr(), x.shape.data(), rank, axes.data(), (int)axes.size(),
@@ -1448,9 +1503,9 @@ bool exec_conv_step(lonnx_graph *g, const Step &s) {
     const NodeDef &c = g->nodes[s.nodes[0]];
     Value res;
     if (!s.b.empty()) {
-        res = lookup(g, s.b);
+        res = lookup_raw(g, s.b);
         if (res.dtype != DT_FLOAT) return false;
-        Value x = lookup(g, c.in.at(0)), w = lookup(g, c.in.at(1));
+        Value x = lookup_raw(g, c.in.at(0)), w = lookup(g, c.in.at(1));  // shapes only: no relayout
         const bool conv_bias = c.in.size() > 2 && !c.in[2].empty();
         if (!conv_bias && w.shape.size() == 4 && x.shape.size() == 4 && channel_bias_shape(res, w.shape[0])) {
             ensure_dev(g, res);
@@ -1540,6 +1595,112 @@ void fold_batchnorm(lonnx_graph *g) {
     for (size_t j = 0; j < g->nodes.size(); ++j)
         if (!drop[j]) kept.push_back(std::move(g->nodes[j]));
     g->nodes.swap(kept);
+}
+
+// Layout pass: the values of a conv chain that may be stored NHWC.  A
+// producer -- a Conv step, or a MaxPool --
+// may write NHWC when every reader of its output takes NHWC: a Conv step
+// reading it as input X (C % 32 == 0, <= 63 taps, group 1: the NHWC gather),
+// a Conv step marked itself reading it as its residual, a marked MaxPool, or
+// a ReduceSum/Mean/Max over axes {2, 3}.  Anything else, or being a graph
+// output, keeps it NCHW.  The marks are permissions: the layout a value got
+// travels with it (Value::nhwc), and lookup() converts for any other reader.
+// With NHWC between them, the convs gather 16-byte rows and store their
+// tiles by TMA; a 1x1 conv needs no transposed copy of its input.
+// LONNX_CONV_NHWC=0 turns the pass off.
+void mark_nhwc(lonnx_graph *g) {
+    g->nhwc_vals.clear();
+    static const bool off = getenv("LONNX_CONV_NHWC") && getenv("LONNX_CONV_NHWC")[0] == '0';
+    if (off) return;
+    enum Role { R_CONV_X, R_CONV_RES, R_POOL, R_REDUCE_HW, R_OTHER };
+    struct Use { int step; Role role; };
+    // a small-network chain step runs its sub-steps one by one unless the
+    // whole chain fits one kernel (batch 1, small): its sub-steps are the
+    // readers and producers (when the chain kernel runs, it reads its input
+    // through lookup() and writes NCHW, which every marked reader takes too)
+    std::vector<const Step *> flat;
+    for (const Step &st : g->steps) {
+        if (st.kind == S_TINY)
+            for (const Step &t : st.sub) flat.push_back(&t);
+        else
+            flat.push_back(&st);
+    }
+    const int ns = (int)flat.size();
+    std::map<std::string, std::vector<Use>> uses;
+    std::vector<std::string> out(ns);       // the candidate producer's output, or empty
+    std::vector<char> x_ok(ns, 0), mark(ns, 0);
+    auto conv_x_ok = [&](const NodeDef &c) {
+        if (c.in.size() < 2 || !g->inits.count(c.in[1])) return false;
+        const Value &W = g->inits.at(c.in[1]);
+        if (W.dtype != DT_FLOAT || W.shape.size() != 4) return false;
+        if (const Attr *a = c.get("group"); a && g->honor_conv_attrs && a->i != 1) return false;
+        const int64_t C = W.shape[1], taps = W.shape[2] * W.shape[3];
+        return C % 32 == 0 && taps <= 63;
+    };
+    auto reduce_hw = [&](const NodeDef &n) {
+        if (n.op != "ReduceMean" && n.op != "ReduceSum" && n.op != "ReduceMax") return false;
+        std::vector<int64_t> axes;
+        if (n.op == "ReduceMean" && g->opset < 13) {
+            if (const Attr *a = n.get("axes")) axes = a->ints;
+        } else if (n.in.size() > 1 && !n.in[1].empty()) {
+            auto it = g->inits.find(n.in[1]);
+            if (it == g->inits.end()) return false;
+            Value v = it->second;
+            ensure_host(g, v);
+            if (v.dtype != DT_INT64) return false;
+            axes.assign(v.h<int64_t>(), v.h<int64_t>() + v.numel());
+        } else if (const Attr *a = n.get("axes")) {
+            axes = a->ints;
+        }
+        std::set<int64_t> ax;
+        for (auto a : axes) ax.insert(a < 0 ? a + 4 : a);
+        return ax == std::set<int64_t>{2, 3};
+    };
+    for (int si = 0; si < ns; ++si) {
+        const Step &st = *flat[si];
+        if (st.kind == S_CONV) {
+            const NodeDef &c = g->nodes[st.nodes[0]];
+            x_ok[si] = conv_x_ok(c);
+            uses[c.in.at(0)].push_back({si, x_ok[si] ? R_CONV_X : R_OTHER});
+            if (!st.b.empty() && !g->inits.count(st.b)) uses[st.b].push_back({si, R_CONV_RES});
+            out[si] = st.y;
+            mark[si] = 1;
+            continue;
+        }
+        if (st.kind == S_NODE && st.nodes.size() == 1) {
+            const NodeDef &n = g->nodes[st.nodes[0]];
+            if (n.op == "MaxPool" && !n.in.empty() && !n.out.empty()) {
+                uses[n.in[0]].push_back({si, R_POOL});
+                out[si] = n.out[0];
+                mark[si] = 1;
+                continue;
+            }
+            if (reduce_hw(n) && !n.in.empty()) {
+                uses[n.in[0]].push_back({si, R_REDUCE_HW});
+                for (size_t k = 1; k < n.in.size(); ++k) uses[n.in[k]].push_back({si, R_OTHER});
+                continue;
+            }
+        }
+        for (int i : st.nodes)
+            for (auto &in : g->nodes[i].in) uses[in].push_back({si, R_OTHER});
+    }
+    const std::set<std::string> outs(g->outputs.begin(), g->outputs.end());
+    for (bool changed = true; changed;) {
+        changed = false;
+        for (int si = 0; si < ns; ++si) {
+            if (!mark[si]) continue;
+            bool ok = !outs.count(out[si]);
+            for (const Use &u : uses[out[si]]) {
+                if (u.role == R_CONV_X || u.role == R_REDUCE_HW) continue;
+                if (u.role == R_CONV_RES && mark[u.step] && x_ok[u.step]) continue;
+                if (u.role == R_POOL && mark[u.step]) continue;
+                ok = false;
+            }
+            if (!ok) { mark[si] = 0; changed = true; }
+        }
+    }
+    for (int si = 0; si < ns; ++si)
+        if (mark[si]) g->nhwc_vals.insert(out[si]);
 }
 
 void build_steps(lonnx_graph *g, bool fuse) {
@@ -1729,6 +1890,7 @@ void build_steps(lonnx_graph *g, bool fuse) {
         i = j;
     }
     g->steps.swap(chained);
+    mark_nhwc(g);
 }
 
 // The chain of a TINY step as one kernel, planned from the run-time shapes;
@@ -1738,8 +1900,9 @@ bool exec_tiny_step(lonnx_graph *g, const Step &s) {
     static const bool off = getenv("LONNX_TINY_CHAIN") && getenv("LONNX_TINY_CHAIN")[0] == '0';
     if (off || s.sub.empty() || s.sub[0].kind != S_CONV) return false;
     const NodeDef &c0 = g->nodes[s.sub[0].nodes[0]];
-    Value x = lookup(g, c0.in.at(0));
-    if (x.dtype != DT_FLOAT || x.shape.size() != 4 || x.shape[0] != 1) return false;
+    // (an NHWC-stored input: a conv chain of a larger batch, run step by step)
+    Value x = lookup_raw(g, c0.in.at(0));
+    if (x.nhwc || x.dtype != DT_FLOAT || x.shape.size() != 4 || x.shape[0] != 1) return false;
     TinyProg p{};
     std::vector<int64_t> cur = x.shape;
     auto numel = [](const std::vector<int64_t> &v) {

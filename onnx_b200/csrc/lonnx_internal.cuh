@@ -102,6 +102,9 @@ struct ConvArgs {
     const float *res = nullptr;
     int tab = 0;  // set by conv_tc: the per-CTA tap table fits (see gemm_tc.cu)
     int nhwc = 0; // x is NHWC and the weights are tap-major: K order (ky, kx, c)
+    // y (and res) NHWC: rows = output pixels, row-major [P, M] -- the GEMM
+    // epilogue (TMA stores; the residual TMA-loaded into its staging blocks)
+    int out_nhwc = 0;
 };
 // A small batch-1 network run as one launch on a cluster of CTAs (tiny.cu):
 // a chain of layers; every CTA holds all weights and the current activation
@@ -123,8 +126,13 @@ struct TinyProg {
 int tiny_chain(lonnx_ctx *ctx, const TinyProg &p, const float *x, float *y);
 // Convs gathered from an NHWC copy of their input (one tap's 32 consecutive
 // channels per K stage, 16-byte copies) with tap-major weights: C a multiple
-// of 32 and a kernel of 2..63 taps.
-bool conv_nhwc_ok(int C, int kh, int kw);
+// of 32 and a kernel of 2..63 taps.  x_nhwc: the input is already NHWC, so a
+// 1x1 kernel gathers from it too (no transpose to pay for).
+bool conv_nhwc_ok(int C, int kh, int kw, bool x_nhwc = false);
+// MaxPool and the H x W reduction (global average pool) over NHWC tensors
+int maxpool2d_nhwc(lonnx_ctx *ctx, const float *x, float *y, int N, int C, int H, int W, int kh, int kw, int sh,
+                   int sw, int pt, int pl, int Ho, int Wo);
+int reduce_hw_nhwc(lonnx_ctx *ctx, int op, const float *x, float *y, int N, int HW, int C);
 // y[N, M, Ho, Wo] = conv(x, W) + bias (+ res) (ReLU if epi); W pre-split
 // into Whi, Wlo [M, ldw] (K = C*kh*kw columns used).  P = N*Ho*Wo.
 int conv_tc(lonnx_ctx *ctx, const ConvArgs &cv, const float *Whi, const float *Wlo, int ldw, const float *bias,
@@ -136,9 +144,13 @@ int split_pad_rows(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int M, 
 int split_rows_tapmajor(lonnx_ctx *ctx, const float *w, float *hi, float *lo, int M, int C, int taps);
 // Conv with optional pre-split weights (whi/wlo [M, ldk], ldk = (K+3)&~3, or
 // nullptr) and an optional residual added before the ReLU.
+// Layouts: x_nhwc / res_nhwc say how x and res are stored; want_out_nhwc
+// asks for an NHWC y, which the tensor-core path gives (*out_nhwc says which
+// layout y got; nullptr: NCHW is required).
 int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, const float *wlo, const float *bias,
            const float *res, float *y, int N, int C, int H, int W, int M, int kh, int kw, int sh, int sw, int pt,
-           int pl, int pb, int pr, int dh, int dw, int group, int relu, int w_tapmajor = 0);
+           int pl, int pb, int pr, int dh, int dw, int group, int relu, int w_tapmajor = 0, int x_nhwc = 0,
+           int res_nhwc = 0, int *out_nhwc = nullptr);
 // Fused attention on tensor cores (dh = 32, S <= 128); LONNX_E_UNSUPPORTED otherwise.
 int attention_tc(lonnx_ctx *ctx, const float *q, const float *k, const float *v, int64_t ld, const float *mask,
                  float *out, int B, int S, int heads, int dh, float scale);

@@ -344,6 +344,73 @@ __global__ void __launch_bounds__(256) k_maxpool3s2(const float *__restrict__ x,
     }
 }
 
+// MaxPool over an NHWC tensor (the conv chain's internal layout, see
+// graph.cpp): a thread takes one output pixel and 4 channels (float4 loads,
+// coalesced along C; C % 4 != 0 falls back to one channel per thread).  Window
+// clipped to the input, max from -inf: the same maxima as the NCHW kernels.
+template <int V>
+__global__ void k_maxpool2d_nhwc(const float *__restrict__ x, float *__restrict__ y, int N, int C, int H, int W,
+                                 int kh, int kw, int sh, int sw, int pt, int pl, int Ho, int Wo) {
+    const int CV = C / V;
+    const int64_t total = (int64_t)N * Ho * Wo * CV;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int cv = (int)(t % CV);
+        int64_t p = t / CV;
+        const int ox = (int)(p % Wo);
+        p /= Wo;
+        const int oy = (int)(p % Ho);
+        const int64_t n = p / Ho;
+        const int r0 = oy * sh - pt, c0 = ox * sw - pl;
+        const int rmin = max(r0, 0), rmax = min(r0 + kh, H), cmin = max(c0, 0), cmax = min(c0 + kw, W);
+        if constexpr (V == 4) {
+            float4 m = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            for (int r = rmin; r < rmax; ++r)
+                for (int c = cmin; c < cmax; ++c) {
+                    const float4 v = __ldg(reinterpret_cast<const float4 *>(x + ((n * H + r) * W + c) * C) + cv);
+                    m = make_float4(fmaxf(m.x, v.x), fmaxf(m.y, v.y), fmaxf(m.z, v.z), fmaxf(m.w, v.w));
+                }
+            reinterpret_cast<float4 *>(y)[t] = m;
+        } else {
+            float m = -INFINITY;
+            for (int r = rmin; r < rmax; ++r)
+                for (int c = cmin; c < cmax; ++c) m = fmaxf(m, __ldg(x + ((n * H + r) * W + c) * C + cv));
+            y[t] = m;
+        }
+    }
+}
+
+// Sum / max / mean over the H x W pixels of an NHWC tensor [N, HW, C] ->
+// [N, C], one thread per (n, c) (coalesced along C), in k_reduce_rows'
+// order: 32 partial sums (element j goes to partial j % 32, each partial
+// sequential in j), then the butterfly of warp_sum over the partials.  The
+// result is bit-identical to reducing the same tensor in NCHW layout.
+__global__ void k_reduce_hw_nhwc(int op, const float *__restrict__ x, float *__restrict__ y, int N, int HW, int C) {
+    const int64_t total = (int64_t)N * C;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = t / C, c = t % C;
+        const float *xp = x + n * HW * C + c;
+        float a[32];
+#pragma unroll
+        for (int l = 0; l < 32; ++l) a[l] = 0.0f;
+        for (int base = 0; base < HW; base += 32) {
+#pragma unroll
+            for (int l = 0; l < 32; ++l) {
+                if (base + l < HW) {
+                    const float v = __ldg(xp + (int64_t)(base + l) * C);
+                    a[l] = op == LONNX_REDUCE_MAX ? fmaxf(a[l], v) : __fadd_rn(a[l], v);
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int l = 0; l < o; ++l) a[l] = op == LONNX_REDUCE_MAX ? fmaxf(a[l], a[l + o]) : __fadd_rn(a[l], a[l + o]);
+        y[t] = reduce_finish(op, a[0], HW);
+    }
+}
+
 }  // namespace
 
 using namespace lonnx;
@@ -362,6 +429,30 @@ int reduce_view(lonnx_ctx *ctx, int op, const float *x, int64_t outer, int64_t r
 }
 int transpose_launch(lonnx_ctx *ctx, const void *x, int elem_bytes, const int64_t *shape, int rank,
                      const int64_t *perm, void *y);
+
+int maxpool2d_nhwc(lonnx_ctx *ctx, const float *x, float *y, int N, int C, int H, int W, int kh, int kw, int sh,
+                   int sw, int pt, int pl, int Ho, int Wo) {
+    const bool v4 = C % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0;
+    const int64_t total = (int64_t)N * Ho * Wo * (v4 ? C / 4 : C);
+    if (total <= 0) return LONNX_OK;
+    const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)ctx->num_sms * 16);
+    if (v4)
+        k_maxpool2d_nhwc<4><<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, y, N, C, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
+    else
+        k_maxpool2d_nhwc<1><<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, y, N, C, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
+
+int reduce_hw_nhwc(lonnx_ctx *ctx, int op, const float *x, float *y, int N, int HW, int C) {
+    const int64_t total = (int64_t)N * C;
+    if (total <= 0) return LONNX_OK;
+    if (HW <= 0) return set_error(LONNX_E_BADARG, "reduce: empty reduction");
+    const int64_t blocks = std::min<int64_t>((total + 127) / 128, (int64_t)ctx->num_sms * 16);
+    k_reduce_hw_nhwc<<<(unsigned)blocks, 128, 0, ctx->stream>>>(op, x, y, N, HW, C);
+    LONNX_CHECK_LAUNCH(ctx);
+    return LONNX_OK;
+}
 }  // namespace lonnx
 
 extern "C" {
