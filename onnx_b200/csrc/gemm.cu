@@ -490,13 +490,14 @@ int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, con
         // copy in scratch, with the weights in tap-major column order
         // (prepared that way, or split so here)
         const bool nhwc = conv_nhwc_ok(C, kh, kw, x_nhwc) && (int64_t)C * H * W < (1ll << 31);
+        const int ldk = (K + 3) & ~3;
         // an NHWC output of a residual conv reads its input NHWC (no tap
         // table); a tile shape that refuses the NHWC output runs once more
         // with an NCHW output rather than on the direct kernel
         const bool onhwc_first = want_out && (!res || nhwc);
         for (int attempt = 0; attempt < (onhwc_first ? 2 : 1); ++attempt) {
             const bool onhwc = onhwc_first && attempt == 0;
-            const int ldk = (K + 3) & ~3;
+            const float *wh = whi, *wl = wlo;
             void *wt = nullptr, *xt = nullptr, *rt = nullptr;
             auto release = [&]() {
                 if (wt) ctx_free(ctx, wt);
@@ -505,39 +506,41 @@ int conv2d(lonnx_ctx *ctx, const float *x, const float *w, const float *whi, con
                 wt = xt = rt = nullptr;
             };
             // one tap: tap-major and channel-major columns are the same order
-            if (!whi || !wlo || ((bool)w_tapmajor != nhwc && kh * kw > 1)) {
+            if (!wh || !wl || ((bool)w_tapmajor != nhwc && kh * kw > 1)) {
                 int rc = ctx_alloc(ctx, (size_t)2 * M * ldk * 4, &wt);
                 if (rc) return rc;
-                whi = (const float *)wt;
-                wlo = whi + (size_t)M * ldk;
-                rc = nhwc ? split_rows_tapmajor(ctx, w, (float *)whi, (float *)wlo, M, C, kh * kw)
-                          : split_pad_rows(ctx, w, (float *)whi, (float *)wlo, M, K, ldk);
+                wh = (const float *)wt;
+                wl = wh + (size_t)M * ldk;
+                rc = nhwc ? split_rows_tapmajor(ctx, w, (float *)wh, (float *)wl, M, C, kh * kw)
+                          : split_pad_rows(ctx, w, (float *)wh, (float *)wl, M, K, ldk);
                 if (rc) { release(); return rc; }
-        }
-        if (nhwc != (bool)x_nhwc) {
-            const int rc = relayout(ctx, x, N, C, H, W, nhwc, &xt);
-            if (rc) { release(); return rc; }
-        }
-        if (res && onhwc != (bool)res_nhwc) {
-            const int rc = relayout(ctx, res, N, M, Ho, Wo, onhwc, &rt);
-            if (rc) { release(); return rc; }
-        }
-        ConvArgs cv;
-        cv.x = xt ? (const float *)xt : x;
-        cv.nhwc = nhwc ? 1 : 0;
-        cv.out_nhwc = onhwc ? 1 : 0;
-        cv.C = C; cv.H = H; cv.W = W; cv.kh = kh; cv.kw = kw; cv.sh = sh; cv.sw = sw;
-        cv.pt = pt; cv.pl = pl; cv.dh = dh; cv.dw = dw; cv.Ho = Ho; cv.Wo = Wo;
-        cv.img_rows = Ho * Wo;
-        cv.res = rt ? (const float *)rt : res;
-        int rc = conv_tc(ctx, cv, whi, wlo, ldk, bias, y, (int)P, M, K, relu ? LONNX_EPI_RELU : LONNX_EPI_NONE);
-        release();
-        if (conv_trace())
-            fprintf(stderr, "[lonnx conv] N%d C%d %dx%d M%d k%dx%d s%d x_nhwc %d gather_nhwc %d out_nhwc %d res %d/%d: %s\n",
-                    N, C, H, W, M, kh, kw, sh, x_nhwc, (int)nhwc, (int)onhwc, res != nullptr, res_nhwc,
-                    rc == LONNX_OK ? "tensor cores" : rc == LONNX_E_UNSUPPORTED ? "unsupported" : "error");
-        if (rc == LONNX_OK && out_nhwc) *out_nhwc = onhwc ? 1 : 0;
-        if (rc != LONNX_E_UNSUPPORTED) return rc;
+            }
+            if (nhwc != (bool)x_nhwc) {
+                const int rc = relayout(ctx, x, N, C, H, W, nhwc, &xt);
+                if (rc) { release(); return rc; }
+            }
+            if (res && onhwc != (bool)res_nhwc) {
+                const int rc = relayout(ctx, res, N, M, Ho, Wo, onhwc, &rt);
+                if (rc) { release(); return rc; }
+            }
+            ConvArgs cv;
+            cv.x = xt ? (const float *)xt : x;
+            cv.nhwc = nhwc ? 1 : 0;
+            cv.out_nhwc = onhwc ? 1 : 0;
+            cv.C = C; cv.H = H; cv.W = W; cv.kh = kh; cv.kw = kw; cv.sh = sh; cv.sw = sw;
+            cv.pt = pt; cv.pl = pl; cv.dh = dh; cv.dw = dw; cv.Ho = Ho; cv.Wo = Wo;
+            cv.img_rows = Ho * Wo;
+            cv.res = rt ? (const float *)rt : res;
+            int rc = conv_tc(ctx, cv, wh, wl, ldk, bias, y, (int)P, M, K, relu ? LONNX_EPI_RELU : LONNX_EPI_NONE);
+            release();
+            if (conv_trace())
+                fprintf(stderr,
+                        "[lonnx conv] N%d C%d %dx%d M%d k%dx%d s%d x_nhwc %d gather %s out_nhwc %d res %d/%d: %s\n", N,
+                        C, H, W, M, kh, kw, sh, x_nhwc, nhwc ? "nhwc" : "nchw", (int)onhwc,
+                        res != nullptr, res_nhwc,
+                        rc == LONNX_OK ? "tensor cores" : rc == LONNX_E_UNSUPPORTED ? "unsupported" : "error");
+            if (rc == LONNX_OK && out_nhwc) *out_nhwc = onhwc ? 1 : 0;
+            if (rc != LONNX_E_UNSUPPORTED) return rc;
         }
     }
     // direct conv: NCHW in and out

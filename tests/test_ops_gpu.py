@@ -454,3 +454,41 @@ def test_conv_tensor_core_dilation_asymmetric_pads(ctx, dil, pads, c, k):
                                    dil[0], dil[1], 1, 0))
     ctx.sync()
     close(y.to_host(), ref.astype(np.float32), atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("c,k,stride,dil,pads,m", [(3, 7, 2, (1, 1), (3, 3, 3, 3), 64),
+                                                   (1, 5, 1, (1, 1), (2, 2, 2, 2), 32),
+                                                   (2, 3, 1, (2, 3), (1, 0, 2, 3), 96),
+                                                   (4, 3, 2, (1, 1), (1, 1, 1, 1), 64),
+                                                   (3, 8, 1, (1, 1), (0, 0, 0, 0), 64)])
+def test_conv_few_channels_tensor_core(ctx, c, k, stride, dil, pads, m):
+    """Convs of 1-4 input channels (the RGB stem's class) on the tensor-core
+    implicit GEMM: K = C x taps is not a multiple of 32, so stages straddle
+    channels and the last one is zero-filled past K; the 8 x 8 kernel (64
+    taps) has more taps than the per-pixel validity mask holds and gathers
+    through the per-stage shuffle path.  Strides, dilations and asymmetric
+    pads against a float64 direct convolution at the 3xTF32 tolerance."""
+    from onnx_b200 import _native as N
+    from onnx_b200.tensor import DeviceTensor
+    rng = np.random.default_rng(c * 100 + k)
+    n, h, w = 5, 45, 38
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((m, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32)
+    b = rng.uniform(-0.1, 0.1, m).astype(np.float32)
+    pt, pl, pb, pr = pads
+    ho = (h + pt + pb - (dil[0] * (k - 1) + 1)) // stride + 1
+    wo = (w + pl + pr - (dil[1] * (k - 1) + 1)) // stride + 1
+    xp = np.pad(x.astype(np.float64), ((0, 0), (0, 0), (pt, pb), (pl, pr)))
+    ref = np.zeros((n, m, ho, wo)) + b.astype(np.float64)[None, :, None, None]
+    for ky in range(k):
+        for kx in range(k):
+            y0, x0 = ky * dil[0], kx * dil[1]
+            patch = xp[:, :, y0:y0 + stride * (ho - 1) + 1:stride, x0:x0 + stride * (wo - 1) + 1:stride]
+            ref += np.einsum("nchw,mc->nmhw", patch, wt[:, :, ky, kx].astype(np.float64))
+    ref = np.maximum(ref, 0.0)
+    dx, dw, db = (DeviceTensor.from_host(ctx, a) for a in (x, wt, b))
+    y = DeviceTensor(ctx, (n, m, ho, wo), np.float32)
+    N.check(N.lib.lonnx_conv2d_f32(ctx.handle, dx.ptr, dw.ptr, db.ptr, y.ptr, n, c, h, w, m, k, k, stride, stride, pt,
+                                   pl, pb, pr, dil[0], dil[1], 1, 1))
+    ctx.sync()
+    close(y.to_host(), ref.astype(np.float32), atol=1e-5, rtol=1e-5)
