@@ -345,37 +345,37 @@ __global__ void __launch_bounds__(256) k_maxpool3s2(const float *__restrict__ x,
 }
 
 // MaxPool over an NHWC tensor (the conv chain's internal layout, see
-// graph.cpp): a thread takes one output pixel and 4 channels (float4 loads,
-// coalesced along C; C % 4 != 0 falls back to one channel per thread).  Window
-// clipped to the input, max from -inf: the same maxima as the NCHW kernels.
+// graph.cpp): blockIdx.y walks the output rows (n, oy), blockIdx.x x
+// threads the row's (ox, 4-channel group) pairs, so the per-thread index
+// math is 32-bit and done once (float4 loads coalesced along C; C % 4 != 0
+// falls back to one channel per thread).  Window clipped to the input, max
+// from -inf: the same maxima as the NCHW kernels.
 template <int V>
 __global__ void k_maxpool2d_nhwc(const float *__restrict__ x, float *__restrict__ y, int N, int C, int H, int W,
                                  int kh, int kw, int sh, int sw, int pt, int pl, int Ho, int Wo) {
-    const int CV = C / V;
-    const int64_t total = (int64_t)N * Ho * Wo * CV;
-    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total;
-         t += (int64_t)gridDim.x * blockDim.x) {
-        const int cv = (int)(t % CV);
-        int64_t p = t / CV;
-        const int ox = (int)(p % Wo);
-        p /= Wo;
-        const int oy = (int)(p % Ho);
-        const int64_t n = p / Ho;
-        const int r0 = oy * sh - pt, c0 = ox * sw - pl;
-        const int rmin = max(r0, 0), rmax = min(r0 + kh, H), cmin = max(c0, 0), cmax = min(c0 + kw, W);
+    const int CV = C / V, per_row = Wo * CV;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= per_row) return;
+    const int cv = i % CV, ox = i / CV;
+    const int c0 = ox * sw - pl, cmin = max(c0, 0), cmax = min(c0 + kw, W);
+    for (int row = blockIdx.y; row < N * Ho; row += gridDim.y) {
+        const int n = row / Ho, oy = row - n * Ho;
+        const int r0 = oy * sh - pt, rmin = max(r0, 0), rmax = min(r0 + kh, H);
+        const float *xn = x + (int64_t)n * H * W * C;
+        float *yr = y + (int64_t)row * Wo * C;
         if constexpr (V == 4) {
             float4 m = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
             for (int r = rmin; r < rmax; ++r)
                 for (int c = cmin; c < cmax; ++c) {
-                    const float4 v = __ldg(reinterpret_cast<const float4 *>(x + ((n * H + r) * W + c) * C) + cv);
+                    const float4 v = __ldg(reinterpret_cast<const float4 *>(xn + ((int64_t)r * W + c) * C) + cv);
                     m = make_float4(fmaxf(m.x, v.x), fmaxf(m.y, v.y), fmaxf(m.z, v.z), fmaxf(m.w, v.w));
                 }
-            reinterpret_cast<float4 *>(y)[t] = m;
+            reinterpret_cast<float4 *>(yr)[i] = m;
         } else {
             float m = -INFINITY;
             for (int r = rmin; r < rmax; ++r)
-                for (int c = cmin; c < cmax; ++c) m = fmaxf(m, __ldg(x + ((n * H + r) * W + c) * C + cv));
-            y[t] = m;
+                for (int c = cmin; c < cmax; ++c) m = fmaxf(m, __ldg(xn + ((int64_t)r * W + c) * C + cv));
+            yr[i] = m;
         }
     }
 }
@@ -433,13 +433,16 @@ int transpose_launch(lonnx_ctx *ctx, const void *x, int elem_bytes, const int64_
 int maxpool2d_nhwc(lonnx_ctx *ctx, const float *x, float *y, int N, int C, int H, int W, int kh, int kw, int sh,
                    int sw, int pt, int pl, int Ho, int Wo) {
     const bool v4 = C % 4 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0;
-    const int64_t total = (int64_t)N * Ho * Wo * (v4 ? C / 4 : C);
-    if (total <= 0) return LONNX_OK;
-    const int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)ctx->num_sms * 16);
+    const int64_t per_row = (int64_t)Wo * (v4 ? C / 4 : C), rows = (int64_t)N * Ho;
+    if (per_row <= 0 || rows <= 0) return LONNX_OK;
+    if (per_row >= (1ll << 31) || rows >= (1ll << 31))
+        return set_error(LONNX_E_UNSUPPORTED, "maxpool2d_nhwc: more than 2^31 outputs per row or rows");
+    const int threads = per_row >= 256 ? 256 : 128;
+    const dim3 grid((unsigned)((per_row + threads - 1) / threads), (unsigned)std::min<int64_t>(rows, 65535));
     if (v4)
-        k_maxpool2d_nhwc<4><<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, y, N, C, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
+        k_maxpool2d_nhwc<4><<<grid, threads, 0, ctx->stream>>>(x, y, N, C, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
     else
-        k_maxpool2d_nhwc<1><<<(unsigned)blocks, 256, 0, ctx->stream>>>(x, y, N, C, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
+        k_maxpool2d_nhwc<1><<<grid, threads, 0, ctx->stream>>>(x, y, N, C, H, W, kh, kw, sh, sw, pt, pl, Ho, Wo);
     LONNX_CHECK_LAUNCH(ctx);
     return LONNX_OK;
 }

@@ -10,6 +10,8 @@ that run them on the GPU with the layout pass on and off.
   tensor-core conv whose output must be NCHW, a MaxPool whose
   output is not NHWC-eligible (its NHWC input converted), a ReduceMax over
   {2, 3} with keepdims, a ReduceSum over channels, a Softmax.
+- pool_shapes: MaxPool 3x3/2 pad 1 and 2x2/2 over NHWC values of odd
+  sizes (17 x 23 -> 9 x 12 -> 4 x 6) between convs, then the H x W mean.
 - projection_residual: two bottlenecks at 14 x 14 (stride-2 1x1 on both
   branches, a 3x3, residual Adds fused into the last 1x1 convs), then the
   H x W mean: the whole chain NHWC.
@@ -71,10 +73,22 @@ def build(case):
         nodes.append(Node("ReduceMean", ["z", "ax23"], ["gap"], {"keepdims": 0}))
         x = rng.uniform(0, 1, (4, 128, 28, 28)).astype(np.float32)
         return GraphDef(nodes, inits, ["x"], ["gap"], opset=18), {"x": x}, ["gap"]
+    if case == "pool_shapes":
+        a = _conv(nodes, inits, rng, "p1", "x", 32, 64, 3, 1)
+        nodes.append(Node("MaxPool", [a], ["mp1"], {"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1],
+                                                    "auto_pad": "NOTSET"}))
+        b = _conv(nodes, inits, rng, "p2", "mp1", 64, 128, 1, 1)
+        nodes.append(Node("MaxPool", [b], ["mp2"], {"kernel_shape": [2, 2], "strides": [2, 2], "pads": [0, 0, 0, 0],
+                                                    "auto_pad": "NOTSET"}))
+        c = _conv(nodes, inits, rng, "p3", "mp2", 128, 64, 3, 1)
+        inits["ax23"] = np.array([2, 3], np.int64)
+        nodes.append(Node("ReduceMean", [c, "ax23"], ["gap"], {"keepdims": 0}))
+        x = rng.standard_normal((3, 32, 17, 23)).astype(np.float32)
+        return GraphDef(nodes, inits, ["x"], ["gap"], opset=18), {"x": x}, ["gap"]
     raise ValueError(case)
 
 
 def has_3x3(case):
     """Whether a 3x3 conv of the case reads an NHWC-eligible value (NCHW
     mode then transposes its input; NHWC mode does not)."""
-    return case in ("resnet50_small", "projection_residual")
+    return case in ("resnet50_small", "projection_residual", "pool_shapes")

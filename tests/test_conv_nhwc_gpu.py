@@ -59,7 +59,7 @@ def _run(case, nhwc):
         return {k: z[k] for k in z.files}
 
 
-@pytest.mark.parametrize("case", ["resnet50_small", "mixed_readers", "projection_residual"])
+@pytest.mark.parametrize("case", ["resnet50_small", "mixed_readers", "projection_residual", "pool_shapes"])
 def test_nhwc_chain_bit_identical_and_vs_oracle(case):
     import nhwc_cases
     on, off = _run(case, True), _run(case, False)
