@@ -74,6 +74,12 @@ internal static unsafe class Native
         long* perm, IntPtr y);
     [DllImport(Lib)] public static extern int lonnx_cast_i64_f32(IntPtr ctx, IntPtr x, IntPtr y, long n);
 
+    // ---- pre-processing before the model (Images.ImageToArrayF, Text.RobertaTokenize padding) ----
+    [DllImport(Lib)] public static extern int lonnx_image_rgba_to_f32(IntPtr ctx, IntPtr rgba, IntPtr y, long nImages,
+        long height, long width);
+    [DllImport(Lib)] public static extern int lonnx_token_batch_pad(IntPtr ctx, IntPtr ids, IntPtr offsets, long batch,
+        long maxLen, long padId, IntPtr idsOut, IntPtr maskOut, IntPtr typeOut);
+
     // ---- fused encoder ops ----
     [DllImport(Lib)] public static extern int lonnx_attention_f32(IntPtr ctx, IntPtr q, IntPtr k, IntPtr v, long ldQkv,
         IntPtr maskadd, IntPtr output, int B, int S, int heads, int dh, float scale);

@@ -182,6 +182,27 @@ LONNX_API int lonnx_transpose(lonnx_ctx *ctx, const void *x, int elem_bytes,
 /* Cast int64 -> float32 element-wise (CPUExecutionProvider.Cast, :451). */
 LONNX_API int lonnx_cast_i64_f32(lonnx_ctx *ctx, const int64_t *x, float *y, int64_t n);
 
+/* ---- pre-processing before the model -------------------------------------
+ * Decoded RGBA8 images [n_images, height, width, 4] (device, 4-byte aligned)
+ * -> float [n_images, 1, height, width], pixel = ((R + G + B) / 3.0f) / 255.0f
+ * with IEEE single divisions: replaces Images.ImageToArrayF
+ * (src/Lokad.Onnx.Data/Images.cs:92-103) after the host has decoded the
+ * file (and, for MNIST inputs, made it grayscale and resized it to 28 x 28,
+ * Images.cs:166-183). */
+LONNX_API int lonnx_image_rgba_to_f32(lonnx_ctx *ctx, const void *rgba, float *y, int64_t n_images,
+                                      int64_t height, int64_t width);
+/* Token batch: the token ids of `batch` sequences concatenated in `ids`
+ * (device), sequence b at [offsets[b], offsets[b + 1]) (device, batch + 1
+ * entries) -> input_ids [batch, max_len] right-padded with pad_id,
+ * attention_mask [batch, max_len] (1 on tokens, 0 on padding) and
+ * token_type_ids [batch, max_len] (0); any output may be NULL; tokens past
+ * max_len are dropped.  Replaces the padding loop of Text.RobertaTokenize
+ * over a string array (src/Lokad.Onnx.Data/Text.cs:126-140), which pads
+ * input_ids with 1 and the other two with 0 up to the longest sequence. */
+LONNX_API int lonnx_token_batch_pad(lonnx_ctx *ctx, const int64_t *ids, const int64_t *offsets, int64_t batch,
+                                    int64_t max_len, int64_t pad_id, int64_t *ids_out, int64_t *mask_out,
+                                    int64_t *type_out);
+
 /* ---- fused encoder ops -------------------------------------------------------
  * Scaled-dot-product attention of one BERT layer, fused: for each batch b and
  * head h, softmax(Q K^T / scale + maskadd[b]) V, with Q, K, V read in place

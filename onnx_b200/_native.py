@@ -53,6 +53,8 @@ _SIGS = {
     "lonnx_gather": (c_int, [c_vp, c_vp, c_int, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "lonnx_transpose": (c_int, [c_vp, c_vp, c_int, i64p, c_int, i64p, c_vp]),
     "lonnx_cast_i64_f32": (c_int, [c_vp, c_vp, c_vp, c_i64]),
+    "lonnx_image_rgba_to_f32": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64]),
+    "lonnx_token_batch_pad": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "lonnx_batchnorm_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_f32, c_vp, c_i64, c_i64, c_i64]),
     "lonnx_attention_f32": (c_int, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_int, c_int, c_int,
                                     c_int, c_f32]),

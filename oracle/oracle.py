@@ -527,6 +527,37 @@ def run_node(node, get, opset=13, honor_conv_attrs=False):
     raise OracleError(f"The operation {op} is not supported by the backend.")
 
 
+# ----------------------------------------------------------------------------
+# Pre-processing before the model (src/Lokad.Onnx.Data)
+# ----------------------------------------------------------------------------
+
+def image_to_array_f(rgba):
+    """Images.ImageToArrayF (Images.cs:92-103): RGBA8 [H, W, 4] ->
+    float [1, 1, H, W], pixel[y, x] = ((R + G + B) / 3.0f) / 255.0f, the
+    byte sum exact, each division one float32 rounding."""
+    a = np.asarray(rgba, dtype=np.uint8)
+    s = a[..., 0].astype(np.int32) + a[..., 1] + a[..., 2]
+    px = (s.astype(np.float32) / np.float32(3.0)) / np.float32(255.0)
+    return px.astype(np.float32).reshape(1, 1, a.shape[0], a.shape[1])
+
+
+def roberta_pad(sequences, pad_id=1):
+    """The padding loop of Text.RobertaTokenize over a string array
+    (Text.cs:126-140): every sequence right-padded to the longest; input_ids
+    with 1, attention_mask ones then zeros, token_type_ids zeros."""
+    seqs = [list(map(int, s)) for s in sequences]
+    maxl = max((len(s) for s in seqs), default=0)
+    ids, mask, types = [], [], []
+    for s in seqs:
+        pad = maxl - len(s)
+        ids.append(s + [pad_id] * pad)
+        mask.append([1] * len(s) + [0] * pad)
+        types.append([0] * maxl)
+    shape = (len(seqs), maxl)
+    return (np.array(ids, np.int64).reshape(shape), np.array(mask, np.int64).reshape(shape),
+            np.array(types, np.int64).reshape(shape))
+
+
 def execute(graph, inputs, honor_conv_attrs=False):
     """Run ``graph`` (nodes in file order) on ``inputs`` (name -> array).
 

@@ -8,7 +8,7 @@ Inputs (paths within the Lokad/Onnx project):
 
 The ONNX protobuf is decoded with the library's own reader
 (onnx_b200/onnx_io.py; the `onnx` package is not installed), and the model
-file itself is copied beside the fixtures for the loader tests.  Images are converted as
+file and the three images are copied beside the fixtures for the loader tests.  Images are converted as
 src/Lokad.Onnx.Data/Images.cs:166-183 does: grayscale, resize to 28x28,
 pixel = mean(R,G,B)/255.  The reference resizes with ImageSharp's default
 resampler; Pillow's bicubic stands in for it (the end-to-end known answers,
@@ -51,7 +51,9 @@ def main(root):
     g, inits = load_model(model)
     arrays = {"init/" + k: v for k, v in inits.items()}
     for d in (4, 2, 5):
-        arrays[f"image/mnist{d}"] = load_image(os.path.join(tdir, "images", f"mnist{d}.png"))
+        png = os.path.join(tdir, "images", f"mnist{d}.png")
+        arrays[f"image/mnist{d}"] = load_image(png)
+        shutil.copyfile(png, os.path.join(here, f"mnist{d}.png"))  # the image files, for the loader tests
     np.savez_compressed(os.path.join(here, "mnist8.npz"), **arrays)
     with open(os.path.join(here, "mnist8_graph.json"), "w") as f:
         json.dump(g, f, indent=1)
